@@ -1,0 +1,510 @@
+// ark_legacy.cu -- the five symbols ARK's Rust code binds today
+// (proyecto_ark/ark01/src/optimizer.rs:20-23, src/ffi.rs:88-115), as CUDA
+// kernels over device pointers, plus the library-wide controls.
+//
+//   ark_asm_adam_step_f16 / ark_asm_adam_step  (asm/opti.s:192-360, :20-177)
+//   ark_asm_grad_clip                          (asm/opti.s:369-432)
+//   ark_quant_f32_to_f16 / ark_dequant_f16_to_f32 (asm/kern.s:879-913, :835-869)
+//
+// All are HBM-streaming kernels: 16-byte vector loads/stores when every
+// pointer is 16-byte aligned, a scalar grid-stride path otherwise (any
+// element alignment works).  Calls run on the legacy default stream (so they
+// are ordered after other default-stream work) and are synchronous by
+// default, so the reference's "returns when done" contract holds for a
+// caller that reads the buffers right after the call.
+#include <cuda_runtime.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <atomic>
+#include <mutex>
+
+#include "ark_device.cuh"
+#include "ark_internal.h"
+
+namespace ark {
+
+// ------------------------------------------------------------ errors
+static thread_local int t_last_error = ARK_OK;
+static std::atomic<uint32_t> g_reported{0};
+
+void set_last_error(int code) { t_last_error = code; }
+
+void legacy_fail(const char* fn, int code, const char* detail) {
+    t_last_error = code;
+    const uint32_t bit = 1u << ((-code) & 31);
+    if (!(g_reported.fetch_or(bit) & bit))
+        fprintf(stderr, "[ark_cuda] %s failed: %s%s%s\n", fn, status_string(code),
+                detail ? ": " : "", detail ? detail : "");
+}
+
+const char* status_string(int s) {
+    switch (s) {
+        case ARK_OK: return "ok";
+        case ARK_E_INVALID_ARG: return "invalid argument";
+        case ARK_E_MISALIGNED: return "buffer not 16-byte aligned";
+        case ARK_E_CUDA: return "CUDA runtime error";
+        case ARK_E_NCCL: return "NCCL error";
+        case ARK_E_TIMEOUT: return "device-side wait timed out";
+        case ARK_E_EARLY_STOP: return "early stop: too many consecutive overflow steps";
+        case ARK_E_NO_DEVICE: return "no usable CUDA device";
+        case ARK_E_UNSUPPORTED: return "unsupported";
+        default: return "unknown status";
+    }
+}
+
+int streaming_grid(const void* kernel, int threads, size_t dyn_smem, uint64_t work_items) {
+    int dev = 0, sms = 148, per_sm = 1;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, dyn_smem);
+    if (per_sm < 1) per_sm = 1;
+    uint64_t full = (uint64_t)sms * (uint64_t)per_sm;
+    uint64_t need = (work_items + threads - 1) / threads;
+    if (need < 1) need = 1;
+    return (int)(need < full ? need : full);
+}
+
+// ------------------------------------------------------------ legacy context
+struct LegacyCtx {
+    std::mutex mu;
+    void* scratch = nullptr;            // grad-clip partials + ticket + result
+    int scratch_blocks = 0;
+};
+
+static LegacyCtx g_ctx[64];
+static std::atomic<int> g_async{0};
+static std::atomic<uint32_t> g_compat{0};
+static std::atomic<cudaStream_t> g_stream{nullptr};   // NULL: legacy default stream
+
+struct ClipResult {
+    float norm;
+    float scale;
+    int apply;
+    int pad;
+};
+
+static int current_ctx(LegacyCtx** out) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return ARK_E_NO_DEVICE;
+    if (dev < 0 || dev >= 64) return ARK_E_NO_DEVICE;
+    *out = &g_ctx[dev];
+    return ARK_OK;
+}
+
+static cudaStream_t legacy_stream(LegacyCtx*) { return g_stream.load(); }
+
+static int finish(LegacyCtx* c) {
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return ARK_E_CUDA;
+    if (!g_async.load()) {
+        e = cudaStreamSynchronize(legacy_stream(c));
+        if (e != cudaSuccess) return ARK_E_CUDA;
+    }
+    return ARK_OK;
+}
+
+constexpr int kT = 256;
+
+// ------------------------------------------------------------ AdamW kernels
+template <typename WT>
+struct WTraits;
+template <>
+struct WTraits<uint16_t> {
+    static __device__ __forceinline__ float load(const uint16_t* p, uint64_t i) { return h2f(p[i]); }
+    static __device__ __forceinline__ void store(uint16_t* p, uint64_t i, float x) { p[i] = f2h(x); }
+};
+template <>
+struct WTraits<float> {
+    static __device__ __forceinline__ float load(const float* p, uint64_t i) { return p[i]; }
+    static __device__ __forceinline__ void store(float* p, uint64_t i, float x) { p[i] = x; }
+};
+
+struct AdamArgs {
+    uint64_t n;
+    float lr, b1, b2, eps, wd;
+    uint32_t t;
+};
+
+// Vector path: 4 elements per item (g, m, v as float4; w as 4 halves or a float4).
+template <typename WT>
+__global__ void __launch_bounds__(kT) adam_vec_kernel(WT* __restrict__ w, const float* __restrict__ g,
+                                                     float* __restrict__ m, float* __restrict__ v,
+                                                     AdamArgs a) {
+    __shared__ AdamK s_k;
+    if (threadIdx.x == 0) s_k = adam_scalars(a.lr, a.b1, a.b2, a.eps, a.wd, a.t);
+    __syncthreads();
+    const AdamK k = s_k;
+    const uint64_t nq = a.n >> 2;
+    const uint64_t stride = (uint64_t)gridDim.x * kT;
+    const float4* g4 = reinterpret_cast<const float4*>(g);
+    float4* m4 = reinterpret_cast<float4*>(m);
+    float4* v4 = reinterpret_cast<float4*>(v);
+    for (uint64_t i = (uint64_t)blockIdx.x * kT + threadIdx.x; i < nq; i += stride) {
+        const float4 gg = ld_stream(g4 + i);
+        float4 mm = ld_stream(m4 + i);
+        float4 vv = ld_stream(v4 + i);
+        float wf[4];
+        if constexpr (sizeof(WT) == 2) {
+            const uint2 wq = __ldcs(reinterpret_cast<const uint2*>(w) + i);
+            wf[0] = h2f(lo16(wq.x)); wf[1] = h2f(hi16(wq.x));
+            wf[2] = h2f(lo16(wq.y)); wf[3] = h2f(hi16(wq.y));
+        } else {
+            const float4 wq = ld_stream(reinterpret_cast<const float4*>(w) + i);
+            wf[0] = wq.x; wf[1] = wq.y; wf[2] = wq.z; wf[3] = wq.w;
+        }
+        wf[0] = adam_elem(wf[0], gg.x, mm.x, vv.x, k, k.decay);
+        wf[1] = adam_elem(wf[1], gg.y, mm.y, vv.y, k, k.decay);
+        wf[2] = adam_elem(wf[2], gg.z, mm.z, vv.z, k, k.decay);
+        wf[3] = adam_elem(wf[3], gg.w, mm.w, vv.w, k, k.decay);
+        st_stream(m4 + i, mm);
+        st_stream(v4 + i, vv);
+        if constexpr (sizeof(WT) == 2) {
+            uint2 o;
+            o.x = pack16(f2h(wf[0]), f2h(wf[1]));
+            o.y = pack16(f2h(wf[2]), f2h(wf[3]));
+            __stcs(reinterpret_cast<uint2*>(w) + i, o);
+        } else {
+            st_stream(reinterpret_cast<float4*>(w) + i, make_float4(wf[0], wf[1], wf[2], wf[3]));
+        }
+    }
+    // ragged tail (n % 4): same arithmetic as the reference's scalar tail
+    if (blockIdx.x == 0 && threadIdx.x < (a.n & 3u)) {
+        const uint64_t i = (nq << 2) + threadIdx.x;
+        float mi = m[i], vi = v[i];
+        const float wn = adam_elem(WTraits<WT>::load(w, i), g[i], mi, vi, k, k.decay);
+        m[i] = mi;
+        v[i] = vi;
+        WTraits<WT>::store(w, i, wn);
+    }
+}
+
+// Scalar path for arbitrarily aligned pointers.
+template <typename WT>
+__global__ void __launch_bounds__(kT) adam_scalar_kernel(WT* w, const float* g, float* m, float* v,
+                                                        AdamArgs a) {
+    __shared__ AdamK s_k;
+    if (threadIdx.x == 0) s_k = adam_scalars(a.lr, a.b1, a.b2, a.eps, a.wd, a.t);
+    __syncthreads();
+    const AdamK k = s_k;
+    const uint64_t stride = (uint64_t)gridDim.x * kT;
+    for (uint64_t i = (uint64_t)blockIdx.x * kT + threadIdx.x; i < a.n; i += stride) {
+        float mi = m[i], vi = v[i];
+        const float wn = adam_elem(WTraits<WT>::load(w, i), g[i], mi, vi, k, k.decay);
+        m[i] = mi;
+        v[i] = vi;
+        WTraits<WT>::store(w, i, wn);
+    }
+}
+
+template <typename WT>
+static int adam_launch(WT* w, const float* g, float* m, float* v, uint64_t n, float lr, float b1,
+                       float b2, float eps, float wd, uint32_t t) {
+    if (n == 0) return ARK_OK;                                  // opti.s:314-315 (n=0: no work)
+    if (!w || !g || !m || !v) return ARK_E_INVALID_ARG;
+    LegacyCtx* c = nullptr;
+    int rc = current_ctx(&c);
+    if (rc) return rc;
+    AdamArgs a{n, lr, b1, b2, eps, wd, t};
+    cudaStream_t s = legacy_stream(c);
+    const bool vec = aligned16(g) && aligned16(m) && aligned16(v) &&
+                     (sizeof(WT) == 2 ? ((reinterpret_cast<uintptr_t>(w) & 7u) == 0) : aligned16(w));
+    if (vec) {
+        const int blocks = streaming_grid(reinterpret_cast<const void*>(adam_vec_kernel<WT>), kT, 0,
+                                          (n >> 2) + 1);
+        adam_vec_kernel<WT><<<blocks, kT, 0, s>>>(w, g, m, v, a);
+    } else {
+        const int blocks = streaming_grid(reinterpret_cast<const void*>(adam_scalar_kernel<WT>), kT,
+                                          0, n);
+        adam_scalar_kernel<WT><<<blocks, kT, 0, s>>>(w, g, m, v, a);
+    }
+    return finish(c);
+}
+
+// ------------------------------------------------------------ grad clip
+// Pass A: per-block sum of squares in double; the last block turns it into
+// {norm, scale, apply}.  Pass B: in-place scale when apply.
+struct ClipScratch {
+    double* blk;
+    unsigned int* ticket;
+    ClipResult* res;
+};
+
+__global__ void __launch_bounds__(kT) clip_norm_kernel(const float* __restrict__ g, uint64_t n,
+                                                      float thr, ClipScratch sc) {
+    __shared__ double s_sum[kT / 32];
+    __shared__ int s_last;
+    double acc = 0.0;
+    const uint64_t stride = (uint64_t)gridDim.x * kT;
+    if (aligned16(g)) {
+        const uint64_t nq = n >> 2;
+        const float4* g4 = reinterpret_cast<const float4*>(g);
+        for (uint64_t i = (uint64_t)blockIdx.x * kT + threadIdx.x; i < nq; i += stride) {
+            const float4 x = __ldcg(g4 + i);
+            acc = __fma_rn((double)x.x, (double)x.x, acc);
+            acc = __fma_rn((double)x.y, (double)x.y, acc);
+            acc = __fma_rn((double)x.z, (double)x.z, acc);
+            acc = __fma_rn((double)x.w, (double)x.w, acc);
+        }
+        if (blockIdx.x == 0 && threadIdx.x < (n & 3u)) {
+            const double x = g[(nq << 2) + threadIdx.x];
+            acc = __fma_rn(x, x, acc);
+        }
+    } else {
+        for (uint64_t i = (uint64_t)blockIdx.x * kT + threadIdx.x; i < n; i += stride) {
+            const double x = g[i];
+            acc = __fma_rn(x, x, acc);
+        }
+    }
+    const double b = block_sum<kT>(acc, s_sum);
+    if (threadIdx.x == 0) sc.blk[blockIdx.x] = b;
+    if (!last_block_arrived(sc.ticket, &s_last)) return;
+    double a = 0.0;
+    for (unsigned int i = threadIdx.x; i < gridDim.x; i += kT) a += __ldcg(sc.blk + i);
+    a = block_sum<kT>(a, s_sum);
+    if (threadIdx.x == 0) {
+        const float norm = __double2float_rn(__dsqrt_rn(a));
+        const int apply = norm > thr;                     // opti.s:402-403 (unordered: no scale)
+        sc.res->norm = norm;
+        sc.res->apply = apply;
+        sc.res->scale = apply ? __fdiv_rn(thr, norm) : 1.0f;  // opti.s:405
+    }
+}
+
+// ARK_COMPAT_CLIP_NEON_FOLD: the reference's exact accumulation order --
+// four f32 lanes, lane l folding fma(x,x,acc) over i = 4k+l (opti.s:383-389),
+// (a0+a1)+(a2+a3) (:391-392), then the sequential tail (:393-398).  One warp;
+// the fold is serial by definition.
+__global__ void clip_neon_fold_kernel(const float* __restrict__ g, uint64_t n, float thr,
+                                      ClipResult* res) {
+    const int lane = threadIdx.x;
+    float acc = 0.0f;
+    const uint64_t n4 = n & ~uint64_t(3);
+    if (lane < 4)
+        for (uint64_t i = lane; i < n4; i += 4) acc = __fmaf_rn(g[i], g[i], acc);
+    const float a1 = __shfl_sync(0xFFFFFFFFu, acc, 1);
+    const float a2 = __shfl_sync(0xFFFFFFFFu, acc, 2);
+    const float a3 = __shfl_sync(0xFFFFFFFFu, acc, 3);
+    if (lane == 0) {
+        float s = __fadd_rn(__fadd_rn(acc, a1), __fadd_rn(a2, a3));
+        for (uint64_t i = n4; i < n; ++i) s = __fmaf_rn(g[i], g[i], s);
+        const float norm = __fsqrt_rn(s);
+        const int apply = norm > thr;
+        res->norm = norm;
+        res->apply = apply;
+        res->scale = apply ? __fdiv_rn(thr, norm) : 1.0f;
+    }
+}
+
+__global__ void __launch_bounds__(kT) clip_scale_kernel(float* __restrict__ g, uint64_t n,
+                                                       const ClipResult* __restrict__ res) {
+    if (!res->apply) return;
+    const float s = res->scale;
+    const uint64_t stride = (uint64_t)gridDim.x * kT;
+    if (aligned16(g)) {
+        const uint64_t nq = n >> 2;
+        float4* g4 = reinterpret_cast<float4*>(g);
+        for (uint64_t i = (uint64_t)blockIdx.x * kT + threadIdx.x; i < nq; i += stride) {
+            float4 x = ld_stream(g4 + i);
+            x.x = __fmul_rn(x.x, s);
+            x.y = __fmul_rn(x.y, s);
+            x.z = __fmul_rn(x.z, s);
+            x.w = __fmul_rn(x.w, s);
+            st_stream(g4 + i, x);
+        }
+        if (blockIdx.x == 0 && threadIdx.x < (n & 3u)) {
+            const uint64_t i = (nq << 2) + threadIdx.x;
+            g[i] = __fmul_rn(g[i], s);
+        }
+    } else {
+        for (uint64_t i = (uint64_t)blockIdx.x * kT + threadIdx.x; i < n; i += stride)
+            g[i] = __fmul_rn(g[i], s);
+    }
+}
+
+static int clip_scratch(LegacyCtx* c, int blocks, ClipScratch* sc) {
+    std::lock_guard<std::mutex> lk(c->mu);
+    if (!c->scratch || c->scratch_blocks < blocks) {
+        if (c->scratch) {
+            cudaStreamSynchronize(legacy_stream(c));
+            cudaFree(c->scratch);
+            c->scratch = nullptr;
+        }
+        const size_t bytes = 256 + 256 + sizeof(double) * (size_t)blocks;
+        if (cudaMalloc(&c->scratch, bytes) != cudaSuccess) return ARK_E_CUDA;
+        if (cudaMemset(c->scratch, 0, bytes) != cudaSuccess) return ARK_E_CUDA;
+        c->scratch_blocks = blocks;
+    }
+    char* b = static_cast<char*>(c->scratch);
+    sc->ticket = reinterpret_cast<unsigned int*>(b);
+    sc->res = reinterpret_cast<ClipResult*>(b + 256);
+    sc->blk = reinterpret_cast<double*>(b + 512);
+    return ARK_OK;
+}
+
+static int clip_launch(float* g, uint64_t n, float thr, float* norm_out) {
+    *norm_out = 0.0f;
+    if (n == 0) return ARK_OK;        // empty: norm 0, no scale
+    if (!g) return ARK_E_INVALID_ARG;
+    LegacyCtx* c = nullptr;
+    int rc = current_ctx(&c);
+    if (rc) return rc;
+    cudaStream_t s = legacy_stream(c);
+    const int blocks = streaming_grid(reinterpret_cast<const void*>(clip_norm_kernel), kT, 0,
+                                      (n >> 2) + 1);
+    ClipScratch sc;
+    rc = clip_scratch(c, blocks, &sc);
+    if (rc) return rc;
+    if (g_compat.load() & ARK_COMPAT_CLIP_NEON_FOLD)
+        clip_neon_fold_kernel<<<1, 32, 0, s>>>(g, n, thr, sc.res);
+    else
+        clip_norm_kernel<<<blocks, kT, 0, s>>>(g, n, thr, sc);
+    const int sblocks = streaming_grid(reinterpret_cast<const void*>(clip_scale_kernel), kT, 0,
+                                       (n >> 2) + 1);
+    clip_scale_kernel<<<sblocks, kT, 0, s>>>(g, n, sc.res);
+    if (cudaGetLastError() != cudaSuccess) return ARK_E_CUDA;
+    ClipResult r;
+    // the norm is the return value: this entry point always waits
+    if (cudaMemcpyAsync(&r, sc.res, sizeof(r), cudaMemcpyDeviceToHost, s) != cudaSuccess)
+        return ARK_E_CUDA;
+    if (cudaStreamSynchronize(s) != cudaSuccess) return ARK_E_CUDA;
+    *norm_out = r.norm;
+    return ARK_OK;
+}
+
+// ------------------------------------------------------------ conversions
+__global__ void __launch_bounds__(kT) quant_kernel(const float* __restrict__ src,
+                                                  uint16_t* __restrict__ dst, uint64_t n, int vec) {
+    const uint64_t stride = (uint64_t)gridDim.x * kT;
+    uint64_t done = 0;
+    if (vec) {
+        const uint64_t n8 = n >> 3;
+        const float4* s4 = reinterpret_cast<const float4*>(src);
+        uint4* d4 = reinterpret_cast<uint4*>(dst);
+        for (uint64_t i = (uint64_t)blockIdx.x * kT + threadIdx.x; i < n8; i += stride) {
+            const float4 a = ld_stream(s4 + 2 * i), b = ld_stream(s4 + 2 * i + 1);
+            uint4 o;
+            o.x = pack16(f2h(a.x), f2h(a.y));
+            o.y = pack16(f2h(a.z), f2h(a.w));
+            o.z = pack16(f2h(b.x), f2h(b.y));
+            o.w = pack16(f2h(b.z), f2h(b.w));
+            st_stream(d4 + i, o);
+        }
+        done = n8 << 3;
+    }
+    for (uint64_t i = done + (uint64_t)blockIdx.x * kT + threadIdx.x; i < n; i += stride)
+        dst[i] = f2h(src[i]);
+}
+
+__global__ void __launch_bounds__(kT) dequant_kernel(const uint16_t* __restrict__ src,
+                                                    float* __restrict__ dst, uint64_t n, int vec) {
+    const uint64_t stride = (uint64_t)gridDim.x * kT;
+    uint64_t done = 0;
+    if (vec) {
+        const uint64_t n8 = n >> 3;
+        const uint4* s4 = reinterpret_cast<const uint4*>(src);
+        float4* d4 = reinterpret_cast<float4*>(dst);
+        for (uint64_t i = (uint64_t)blockIdx.x * kT + threadIdx.x; i < n8; i += stride) {
+            const uint4 q = ld_stream(s4 + i);
+            st_stream(d4 + 2 * i, make_float4(h2f(lo16(q.x)), h2f(hi16(q.x)), h2f(lo16(q.y)),
+                                              h2f(hi16(q.y))));
+            st_stream(d4 + 2 * i + 1, make_float4(h2f(lo16(q.z)), h2f(hi16(q.z)),
+                                                  h2f(lo16(q.w)), h2f(hi16(q.w))));
+        }
+        done = n8 << 3;
+    }
+    for (uint64_t i = done + (uint64_t)blockIdx.x * kT + threadIdx.x; i < n; i += stride)
+        dst[i] = h2f(src[i]);
+}
+
+static int convert_launch(const void* src, void* dst, uint64_t n, bool quant) {
+    if (n == 0) return ARK_OK;
+    if (!src || !dst) return ARK_E_INVALID_ARG;
+    LegacyCtx* c = nullptr;
+    int rc = current_ctx(&c);
+    if (rc) return rc;
+    const int vec = aligned16(src) && aligned16(dst);
+    cudaStream_t s = legacy_stream(c);
+    if (quant) {
+        const int blocks = streaming_grid(reinterpret_cast<const void*>(quant_kernel), kT, 0,
+                                          vec ? (n >> 3) + 1 : n);
+        quant_kernel<<<blocks, kT, 0, s>>>(static_cast<const float*>(src),
+                                            static_cast<uint16_t*>(dst), n, vec);
+    } else {
+        const int blocks = streaming_grid(reinterpret_cast<const void*>(dequant_kernel), kT, 0,
+                                          vec ? (n >> 3) + 1 : n);
+        dequant_kernel<<<blocks, kT, 0, s>>>(static_cast<const uint16_t*>(src),
+                                              static_cast<float*>(dst), n, vec);
+    }
+    return finish(c);
+}
+
+}  // namespace ark
+
+using namespace ark;
+
+extern "C" {
+
+void ark_asm_adam_step_f16(uint16_t* w, const float* g, float* m, float* v, uint64_t n, float lr,
+                           float beta1, float beta2, float eps, float wd, uint32_t t) {
+    const int rc = adam_launch<uint16_t>(w, g, m, v, n, lr, beta1, beta2, eps, wd, t);
+    if (rc) legacy_fail("ark_asm_adam_step_f16", rc, nullptr); else set_last_error(ARK_OK);
+}
+
+void ark_asm_adam_step(float* w, const float* g, float* m, float* v, uint64_t n, float lr,
+                       float beta1, float beta2, float eps, float wd, uint32_t t) {
+    const int rc = adam_launch<float>(w, g, m, v, n, lr, beta1, beta2, eps, wd, t);
+    if (rc) legacy_fail("ark_asm_adam_step", rc, nullptr); else set_last_error(ARK_OK);
+}
+
+float ark_asm_grad_clip(float* grads, uint64_t n, float threshold) {
+    float norm = 0.0f;
+    const int rc = clip_launch(grads, n, threshold, &norm);
+    if (rc) {
+        legacy_fail("ark_asm_grad_clip", rc, nullptr);
+        return __builtin_nanf("");
+    }
+    set_last_error(ARK_OK);
+    return norm;
+}
+
+void ark_quant_f32_to_f16(const float* src, uint16_t* dst, uint64_t n) {
+    const int rc = convert_launch(src, dst, n, true);
+    if (rc) legacy_fail("ark_quant_f32_to_f16", rc, nullptr); else set_last_error(ARK_OK);
+}
+
+void ark_dequant_f16_to_f32(const uint16_t* src, float* dst, uint64_t n) {
+    const int rc = convert_launch(src, dst, n, false);
+    if (rc) legacy_fail("ark_dequant_f16_to_f32", rc, nullptr); else set_last_error(ARK_OK);
+}
+
+int ark_cuda_last_error(void) { return t_last_error; }
+
+const char* ark_cuda_strerror(int status) { return status_string(status); }
+
+int ark_cuda_set_compat(uint32_t flags) {
+    if (flags & ~ARK_COMPAT_CLIP_NEON_FOLD) return ARK_E_INVALID_ARG;
+    g_compat.store(flags);
+    return ARK_OK;
+}
+
+int ark_cuda_legacy_set_stream(void* stream) {
+    g_stream.store(reinterpret_cast<cudaStream_t>(stream));
+    return ARK_OK;
+}
+
+int ark_cuda_legacy_set_async(int async) {
+    g_async.store(async ? 1 : 0);
+    return ARK_OK;
+}
+
+int ark_cuda_legacy_sync(void) {
+    LegacyCtx* c = nullptr;
+    int rc = current_ctx(&c);
+    if (rc) return rc;
+    return cudaStreamSynchronize(legacy_stream(c)) == cudaSuccess ? ARK_OK : ARK_E_CUDA;
+}
+
+uint32_t ark_cuda_abi_version(void) { return ARK_OPT_ABI_VERSION; }
+
+}  // extern "C"

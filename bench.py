@@ -1,0 +1,358 @@
+"""Benchmark of the ARK optimizer hot path on B200.
+
+Workload: the EKO-237M full optimizer step --
+finite check + unscale + global L2 norm and clip + AdamW (FP16 weights in
+place, FP32 m/v) + loss-scale update -- over all 236,959,488 parameters,
+ZeRO-1-sharded over the N GPUs of one node (one process per GPU).  Inputs
+are seeded synthetic tensors with the BASELINE distributions, generated on
+the device.  The optimizer state (5.2 GB at N=1) is far larger than the
+126 MB L2, so no flush is needed between steps.
+
+Metric: step time and achieved HBM bandwidth, counted as 24 algorithmic
+bytes per parameter per step (pass 1 reads the 2-byte gradient; pass 2
+reads g, w, m, v and writes w, m, v: 22 bytes); value = 24 * N_params /
+step time, whole job (all GPUs).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+  (N > 1: python -m torch.distributed.run --nproc-per-node N bench.py --gpus N ...)
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "AdamW+clip step time & achieved HBM GB/s, EKO-237M fp16, 1/2/4/8 B200"
+BYTES_PER_PARAM = 24          # algorithmic bytes per parameter per step
+PASS2_BYTES_PER_PARAM = 22    # dominant kernel: pass 2
+PASS1_BYTES_PER_PARAM = 2
+SEED = 20261201
+EKO_HPARAMS = dict(lr=3e-4, beta1=0.9, beta2=0.95, eps=1e-8, weight_decay=0.1, grad_clip=1.0)
+START_STEP = 1000             # configs[0]: "step 1000"
+LOSS_SCALE = 65536.0
+
+
+def measured_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured (MEASURED_PEAKS.json hbm_gbs)"
+    except Exception:
+        return 6650.0, "fallback 6.65 TB/s (MEASURED_PEAKS.json absent)"
+
+
+def pass2_traffic_per_param():
+    """DRAM bytes per parameter of the pass-2 kernel from the committed ncu
+    summary (profiles/pass2_adamw_eko.md, line 'dram_bytes_per_param: X')."""
+    p = os.path.join(ROOT, "profiles", "pass2_adamw_eko.md")
+    try:
+        for line in open(p):
+            if line.strip().startswith("dram_bytes_per_param:"):
+                return float(line.split(":")[1].split()[0])
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms while running."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(prefix="ark_clocks_", suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.proc or not self.path:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        for line in open(self.path):
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(rows)}
+
+
+def cpu_reference_step_setup(L, threads):
+    """The reference's own CPU path (per-tensor, FP32 grads) on this host."""
+    from oracle import oracle
+    n = L.n
+    w16 = oracle.synth_f16(n, 0, SEED, 1, 0.02)
+    g32 = oracle.dequant(oracle.synth_f16(n, 0, SEED, 2, 1e-3, LOSS_SCALE))
+    m = oracle.synth_f32(n, 0, SEED, 3, 1e-4)
+    v = oracle.synth_f32(n, 0, SEED, 4, 1e-3, square=True)
+    g_fresh = g32.copy()
+    ts = (oracle.Tensor * L.n_tensors)()
+    # reference order (optimizer.rs:185-227) over views into the flat arrays
+    for i, t in enumerate(L.tensors):
+        o = L.offsets[t.name]
+        ts[i] = oracle.Tensor(w16[o:].ctypes.data, g32[o:].ctypes.data, m[o:].ctypes.data,
+                              v[o:].ctypes.data, t.numel, EKO_HPARAMS["weight_decay"] if t.decay
+                              else 0.0, 0 if t.name == "gamma_final" else 1)
+    st = oracle.make_state(LOSS_SCALE, opt_step=START_STEP - 1)
+    keep = (w16, g32, m, v, g_fresh)
+
+    def step():
+        np.copyto(g32, g_fresh)           # fresh grads each step (the backward's job; untimed)
+        t0 = time.perf_counter()
+        rc = oracle.lib().ork_ref_step_tensors(
+            ts, L.n_tensors, st, EKO_HPARAMS["lr"], EKO_HPARAMS["beta1"], EKO_HPARAMS["beta2"],
+            EKO_HPARAMS["eps"], EKO_HPARAMS["grad_clip"], 2.0 ** 24, 2000, threads)
+        dt = time.perf_counter() - t0
+        assert rc == 0
+        return dt
+
+    return step, keep
+
+
+def run_reference(args):
+    """--impl reference: the reference's CPU optimizer path (oracle port of
+    opti.s + optimizer.rs + training.rs, per tensor, FP32 grads) with every
+    host thread, on the same EKO-237M workload."""
+    rank = int(os.environ.get("RANK", 0))
+    if rank != 0:
+        return
+    from ark_b200 import layout
+    from oracle import oracle
+    oracle.build()
+    threads = oracle.lib().ork_max_threads()
+    L = layout.eko_layout()
+    step, _keep = cpu_reference_step_setup(L, threads)
+    for _ in range(args.warmup):
+        step()
+    times = [step() for _ in range(args.steps)]
+    t = statistics.mean(times)
+    value = BYTES_PER_PARAM * L.n / t / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(t * 1e3, 3), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, BASELINE distributions)",
+        "config": {"workload": "EKO-237M full optimizer step (BASELINE configs[0])",
+                   "params": L.n, "tensors": L.n_tensors, "grads": "fp32 (reference layout)"},
+        "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads,
+                         "kind": "port",
+                         "sample": f"full EKO-237M step x {args.steps} (all {L.n} params, "
+                                   f"{L.n_tensors} tensors)"},
+        "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def cpu_baseline_single_thread(L, budget_s=15.0):
+    """1-thread reference path (faithful to the reference's single thread)."""
+    from oracle import oracle
+    oracle.build()
+    step, _keep = cpu_reference_step_setup(L, 1)
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while not times or (time.perf_counter() < t_end and len(times) < 3):
+        times.append(step())
+    t = min(times)
+    return {"value": round(BYTES_PER_PARAM * L.n / t / 1e9, 3), "unit": "GB/s", "cores": 1,
+            "kind": "port",
+            "sample": f"full EKO-237M step x {len(times)} on 1 thread, best "
+                      f"{t * 1e3:.0f} ms/step"}
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    import ark_b200 as ab
+    from ark_b200 import dist as adist
+    from ark_b200 import layout, synth
+
+    rank, world, local = adist.env_rank_world()
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    L = layout.eko_layout()
+    comm = adist.nccl_comm(rank, world, local) if world > 1 else None
+    adam = ab.AdamConfig(**EKO_HPARAMS)
+    scale = ab.LossScaleConfig(init=LOSS_SCALE, every=2000, max=2.0 ** 24)
+    stream = torch.cuda.current_stream(dev)
+    opt = ab.Optimizer(L, adam, scale, device=local, rank=rank, world=world, comm=comm,
+                       stream=stream, constant_lr=True, initial_step=START_STEP - 1,
+                       use_graph=args.graph)
+    lo, n = opt.lo, opt.n
+    w16, g16, m, v = synth.make_state(n, lo, SEED, dev, loss_scale=LOSS_SCALE)
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    def max_over_ranks(x):
+        if world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        opt.step_all(w16, g16, m, v)
+    torch.cuda.synchronize()
+
+    # ---- timed region: K steps, kernel events recorded by the library ----
+    if not args.graph:
+        opt.profile_begin(args.steps)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        barrier()
+        torch.cuda.synchronize()
+        ev0.record(stream)
+        for _ in range(args.steps):
+            opt.step_all(w16, g16, m, v)
+        ev1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+    step_ms_local = ev0.elapsed_time(ev1) / args.steps
+    prof = None if args.graph else opt.profile_read(args.steps)
+    step_ms = max_over_ranks(step_ms_local)
+    st = opt.status()
+    assert st["last_overflow"] == 0 and st["opt_step"] == START_STEP - 1 + args.warmup + args.steps
+
+    # ---- e2e: host grads -> device, step, status back, every step ----
+    g_host = torch.empty(n, dtype=torch.float16, pin_memory=True)
+    g_host.copy_(g16.cpu())
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        opt.upload_grads(g16, g_host)
+        opt.step_all(w16, g16, m, v)
+        opt.status()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+
+    # ---- roofline of the dominant kernel (pass 2) ----
+    peak, peak_src = measured_peak()
+    roof = None
+    if prof is not None and len(prof):
+        p1 = float(np.mean(prof[:, 0]))
+        ex = float(np.mean(prof[:, 1]))
+        p2 = float(np.mean(prof[:, 2]))
+        p2_max = max_over_ranks(p2)
+        achieved = PASS2_BYTES_PER_PARAM * n / (p2 * 1e-3) / 1e9
+        tpp = pass2_traffic_per_param()
+        roof = {"kernel": "ark::pass2_kernel (fused unscale+clip+AdamW)", "bound": "hbm",
+                "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "peak_source": peak_src,
+                "traffic": round(tpp * n) if tpp else None,
+                "algorithmic_bytes_per_launch": PASS2_BYTES_PER_PARAM * n,
+                "pass2_ms": round(p2, 4), "pass2_ms_max_rank": round(p2_max, 4),
+                "pass1_ms": round(p1, 4),
+                "pass1_gbs": round(PASS1_BYTES_PER_PARAM * n / (p1 * 1e-3) / 1e9, 1),
+                "exchange_ms": round(ex, 4)}
+    clk = clocks.summary()
+    geom = opt.geometry()
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline_single_thread(L)
+
+    if rank == 0:
+        value = BYTES_PER_PARAM * L.n / (step_ms * 1e-3) / 1e9
+        e2e_val = BYTES_PER_PARAM * L.n / (e2e_ms * 1e-3) / 1e9
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(step_ms, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded splitmix64 + Irwin-Hall normals with the BASELINE "
+                    "distributions, generated on the device)",
+            "config": {"workload": "EKO-237M full optimizer step (BASELINE configs[0])",
+                       "params": L.n, "params_per_gpu": n, "tensors": L.n_tensors,
+                       "parallelism": f"zero1-dp{world}", "t": START_STEP,
+                       "loss_scale": LOSS_SCALE, "clip": "active",
+                       "bytes_per_param": BYTES_PER_PARAM, "graph": bool(args.graph),
+                       "l2": "inputs larger than L2 (state %.2f GB/GPU vs 126 MB L2); no flush"
+                             % (n * 12 / 1e9),
+                       "geometry": geom},
+            "roofline": roof,
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e_val, 2), "unit": "GB/s", "ms_per_step": round(e2e_ms, 3),
+                    "h2d_bytes_per_step": 2 * L.n, "d2h_bytes_per_step": 64 * world,
+                    "path": "Optimizer.upload_grads (pinned host fp16 grads) + step_all + "
+                            "status() per step, through the C ABI"},
+            "gpu_launches": 2 * args.steps,
+            "clocks": clk,
+        }
+        print(json.dumps(line), flush=True)
+    opt.close()
+    if comm:
+        adist.nccl_comm_destroy(comm)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--graph", action="store_true", help="replay the step as a CUDA graph")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,195 @@
+"""The fused whole-step API (ark_cuda_opt_*) on a B200 against the CPU
+oracle: finite check, unscale, global norm and clip, AdamW over the flat
+decayed-first layout, and the loss-scale state machine, step by step.
+Flags and scale sequences are compared exactly; the norm within 1e-5
+relative (it is bit-identical in practice); w, m, v bit for bit."""
+import numpy as np
+import pytest
+import torch
+
+import ark_b200 as ab
+from ark_b200 import layout, synth
+from gpu_util import dev, first_diff, host, same_f16, same_f32
+
+pytestmark = pytest.mark.gpu
+
+SEED = 1234
+STATE_KEYS = ("loss_scale", "opt_step", "clean_steps", "consecutive_nans", "skipped_steps",
+              "last_overflow", "early_stop")
+
+
+def oracle_bufs(oracle, n, lo, seed, scale, heavy=False, grad_stream=synth.STREAM_G):
+    w = oracle.synth_f16(n, lo, seed, synth.STREAM_W, 0.02)
+    g = oracle.synth_f16(n, lo, seed, grad_stream, 1e-3, scale,
+                         synth.HEAVY_EVERY if heavy else 0, synth.HEAVY_MULT if heavy else 1.0)
+    m = oracle.synth_f32(n, lo, seed, synth.STREAM_M, 1e-4)
+    v = oracle.synth_f32(n, lo, seed, synth.STREAM_V, 1e-3, square=True)
+    return w, g, m, v
+
+
+def check_state(dev_st, ost, where=""):
+    for k in STATE_KEYS:
+        assert dev_st[k] == getattr(ost, k), f"{where}: {k} {dev_st[k]} vs {getattr(ost, k)}"
+    if not ost.last_overflow and ost.opt_step:
+        rel = abs(dev_st["last_norm"] - ost.last_norm) / max(ost.last_norm, 1e-30)
+        assert rel <= 1e-5, f"{where}: norm {dev_st['last_norm']} vs {ost.last_norm}"
+        assert dev_st["last_lr"] == ost.last_lr
+
+
+def run_steps(oracle, L, *, steps, scale0=65536.0, initial_step=0, shard=None, compat=False,
+              inject=None, lr_table=(3e-4,), use_graph=False, adam=None, scale_cfg=None,
+              fresh_grads=True, max_nans=200, heavy=False):
+    adam = adam or ab.AdamConfig(lr=3e-4, beta1=0.9, beta2=0.95, eps=1e-8, weight_decay=0.1,
+                                 grad_clip=1.0)
+    scale_cfg = scale_cfg or ab.LossScaleConfig(init=scale0, every=50, max=2.0 ** 24,
+                                                max_consecutive_nans=max_nans)
+    opt = ab.Optimizer(L, adam, scale_cfg, lr_table=np.asarray(lr_table, np.float32),
+                       initial_step=initial_step, shard=shard, compat_gamma_final_unscaled=compat,
+                       use_graph=use_graph)
+    lo, n = opt.lo, opt.n
+    w, g, m, v = oracle_bufs(oracle, n, lo, SEED, scale0, heavy)
+    dw, dg, dm, dv = dev(w), dev(g), dev(m), dev(v)
+    gf = L.gamma_final_range()
+    cfg = oracle.make_cfg(beta1=adam.beta1, beta2=adam.beta2, eps=adam.eps,
+                          weight_decay=adam.weight_decay, grad_clip=adam.grad_clip,
+                          scale_backoff=scale_cfg.backoff, scale_growth=scale_cfg.growth,
+                          scale_min=scale_cfg.min, scale_max=scale_cfg.max,
+                          scale_every=scale_cfg.every,
+                          max_consecutive_nans=scale_cfg.max_consecutive_nans,
+                          lr_table=lr_table, n_decay=L.n_decay,
+                          keep_lo=gf[0] if compat else 0, keep_hi=gf[1] if compat else 0)
+    ost = oracle.make_state(scale0, opt_step=initial_step)
+    for k in range(1, steps + 1):
+        if fresh_grads and k > 1:
+            sc = np.float32(ost.loss_scale)
+            g = oracle.synth_f16(n, lo, SEED, synth.GRAD_STEP_STREAM_BASE + k, 1e-3, sc)
+            synth.fill_f16(dg, lo, SEED, synth.GRAD_STEP_STREAM_BASE + k, 1e-3, mult=float(sc))
+        if inject and k in inject:
+            idx = oracle.lib().ork_inject_index(SEED, k, n)
+            g[idx] = inject[k]
+            dg.view(torch.int16)[idx] = int(np.int16(np.uint16(inject[k]).view(np.int16)))
+        s, bad = oracle.partial_f16(cfg, ost, g, lo)
+        oracle.apply_f16(cfg, ost, w, g, m, v, lo, s, bad)
+        opt.step_all(dw, dg, dm, dv)
+        check_state(opt.status(), ost, f"step {k}")
+    hw, hm, hv = host(dw), host(dm), host(dv)
+    assert same_f16(hw, w), f"w first diff at {first_diff(hw, w)}"
+    assert same_f32(hm, m), f"m first diff at {first_diff(hm, m)}"
+    assert same_f32(hv, v), f"v first diff at {first_diff(hv, v)}"
+    st = opt.status()
+    opt.close()
+    return st, ost
+
+
+def tiny():
+    return layout.decoder_layout("tiny", 3, 32, 72, 97)
+
+
+def test_tiny_decoder_multi_step(oracle):
+    st, _ = run_steps(oracle, tiny(), steps=6, inject={3: 0x7E00})
+    assert st["opt_step"] == 5 and st["skipped_steps"] == 1
+
+
+def test_compat_gamma_final_unscaled(oracle):
+    st, _ = run_steps(oracle, tiny(), steps=3, compat=True)
+    assert st["opt_step"] == 3
+
+
+@pytest.mark.parametrize("shard", [(1024, 8231), (0, 7), (128, 128 + 8 * 37)])
+def test_shard_offsets_and_ragged_sizes(oracle, shard):
+    L = tiny()
+    run_steps(oracle, L, steps=2, shard=shard)
+
+
+def test_warmup_lr_table_and_resume_step(oracle):
+    tab = ab.lr_schedule(ab.AdamConfig(lr=1e-3, warmup_steps=10), 40)
+    run_steps(oracle, tiny(), steps=4, lr_table=tab, initial_step=7)
+
+
+def test_no_clip_path(oracle):
+    adam = ab.AdamConfig(lr=3e-4, beta1=0.9, beta2=0.95, eps=1e-8, weight_decay=0.1,
+                         grad_clip=1e9)
+    st, _ = run_steps(oracle, tiny(), steps=2, adam=adam)
+    assert st["last_clip_coef"] == 1.0
+
+
+def test_graph_replay_matches(oracle):
+    run_steps(oracle, tiny(), steps=4, use_graph=True, inject={2: 0x7C00})
+
+
+def test_early_stop(oracle):
+    inject = {k: 0xFC00 for k in range(1, 7)}
+    st, ost = run_steps(oracle, tiny(), steps=6, inject=inject, max_nans=3)
+    assert st["early_stop"] == 1 and ost.early_stop == 1
+    assert st["consecutive_nans"] == 4 and st["opt_step"] == 0
+
+
+def test_eko_full_step_bit_exact(oracle):
+    """EKO-237M full optimizer step, t = 1000, scale 65536."""
+    st, ost = run_steps(oracle, layout.eko_layout(), steps=1, initial_step=999, fresh_grads=False)
+    assert st["opt_step"] == 1000 and st["last_clip_coef"] < 1.0
+    assert st["last_norm"] == ost.last_norm
+
+
+def test_trajectory_200_steps_flags_and_scale(oracle):
+    """200 steps of fresh seeded grads with +inf/NaN injected at
+    steps 17, 18, 90; scale init 65536, backoff 0.5, growth x2 every 50
+    clean steps, max 2^24.  Every element checked at 1M params; the
+    flags/scale sequence additionally at the full EKO size below."""
+    inject = {17: 0x7C00, 18: 0x7E00, 90: 0x7C00}
+    st, ost = run_steps(oracle, layout.flat_layout(1_000_003), steps=200, inject=inject)
+    assert st["skipped_steps"] == 3 and st["opt_step"] == 197
+
+
+def test_trajectory_200_steps_eko_size(oracle):
+    L = layout.eko_layout()
+    scale_cfg = ab.LossScaleConfig(init=65536.0, every=50, max=2.0 ** 24)
+    adam = ab.AdamConfig(lr=3e-4, beta1=0.9, beta2=0.95, eps=1e-8, weight_decay=0.1,
+                         grad_clip=1.0)
+    opt = ab.Optimizer(L, adam, scale_cfg, constant_lr=True, initial_step=999)
+    dw, dg, dm, dv = synth.make_state(L.n, 0, SEED, "cuda", loss_scale=65536.0)
+    cfg = oracle.make_cfg(scale_every=50, scale_max=2.0 ** 24)
+    ost = oracle.make_state(65536.0, opt_step=999)
+    w, g, m, v = oracle_bufs(oracle, 8, 0, SEED, 1.0)
+    seq_dev, seq_ref = [], []
+    inject = {17: 0x7C00, 18: 0x7E00, 90: 0x7C00}
+    for k in range(1, 201):
+        sc = opt.status()["loss_scale"]
+        synth.fill_grads(dg, 0, SEED, sc, grad_stream=synth.GRAD_STEP_STREAM_BASE + k)
+        if k in inject:
+            idx = oracle.lib().ork_inject_index(SEED, k, L.n)
+            dg.view(torch.int16)[idx] = int(np.uint16(inject[k]).view(np.int16))
+        opt.step_all(dw, dg, dm, dv)
+        s = opt.status()
+        seq_dev.append((s["last_overflow"], s["loss_scale"], s["opt_step"], s["clean_steps"]))
+        oracle.apply_f16(cfg, ost, w, g, m, v, 0, 1.0, 1 if k in inject else 0)
+        seq_ref.append((ost.last_overflow, ost.loss_scale, ost.opt_step, ost.clean_steps))
+    assert seq_dev == seq_ref
+    assert [k + 1 for k, s in enumerate(seq_dev) if s[0]] == [17, 18, 90]
+    opt.close()
+
+
+def test_bad_arguments():
+    import ctypes
+    opt = ab.Optimizer(tiny(), constant_lr=True)
+    t = torch.zeros(opt.n + 8, dtype=torch.float16, device="cuda")
+    f = torch.zeros(opt.n + 8, dtype=torch.float32, device="cuda")
+    rc = ab.lib().ark_cuda_opt_step(opt._h, t.data_ptr() + 2, t.data_ptr(), f.data_ptr(),
+                                    f.data_ptr())
+    assert rc == -2
+    cfg = ab._lib.OptCfg()
+    h = ctypes.c_void_p()
+    assert ab.lib().ark_cuda_opt_init(ctypes.byref(cfg), ctypes.byref(h)) == -1
+    opt.close()
+
+
+def test_profile_events():
+    L = layout.flat_layout(10_000_000)
+    opt = ab.Optimizer(L, constant_lr=True)
+    bufs = synth.make_state(L.n, 0, 3, "cuda")
+    opt.profile_begin(3)
+    for _ in range(3):
+        opt.step_all(*bufs)
+    prof = opt.profile_read(3)
+    assert prof.shape == (3, 3) and (prof[:, 0] > 0).all() and (prof[:, 2] > 0).all()
+    opt.close()
