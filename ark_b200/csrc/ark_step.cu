@@ -64,14 +64,28 @@ constexpr int kUnroll1 = 4;   // 16-byte gradient vectors in flight per thread, 
 constexpr int kUnroll2 = 2;   // 8-element groups in flight per thread, pass 2
 
 // --------------------------------------------------------------- pass 1
-__device__ __forceinline__ void accum8(uint4 q, uint64_t gi0, float inv, uint64_t keep_lo,
-                                       uint64_t keep_hi, double& acc, unsigned long long& bad) {
+// Exact FP16 -> FP64 widening (one conversion instruction).
+__device__ __forceinline__ double h2d(uint16_t h) {
+    double d;
+    asm("cvt.f64.f16 %0, %1;" : "=d"(d) : "h"(h));
+    return d;
+}
+
+// Max of |h| over the packed halves seen so far (SIMD on 2 x 16 bits); a
+// value >= 0x7C00 in either half means an inf or NaN was present.
+__device__ __forceinline__ uint32_t absmax2(uint32_t acc, uint32_t w) {
+    return __vmaxu2(acc, w & 0x7FFF7FFFu);
+}
+
+// General path: u = fp32(h) * inv rounded to f32, exactly as training.rs:308
+// computes the unscaled gradient, then u*u accumulated in double.
+__device__ __forceinline__ void accum8_general(uint4 q, uint64_t gi0, float inv, uint64_t keep_lo,
+                                               uint64_t keep_hi, double& acc) {
     const uint32_t w[4] = {q.x, q.y, q.z, q.w};
     const bool keep_any = (gi0 + 8 > keep_lo) && (gi0 < keep_hi);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
         const uint16_t h = (j & 1) ? hi16(w[j >> 1]) : lo16(w[j >> 1]);
-        bad += ((h & 0x7C00u) == 0x7C00u);
         const float f = h2f(h);
         const bool keep = keep_any && (gi0 + j >= keep_lo) && (gi0 + j < keep_hi);
         const float u = keep ? f : __fmul_rn(f, inv);
@@ -80,13 +94,39 @@ __device__ __forceinline__ void accum8(uint4 q, uint64_t gi0, float inv, uint64_
     }
 }
 
+// Power-of-two loss scale (the only kind the state machine produces from a
+// power-of-two init, backoff and growth): fp32(h) * inv is exact, so the sum
+// of squared unscaled gradients is inv^2 * sum(h^2), with h^2 exact in
+// double.  Elements in the kept range (compat mode) go to acc_k unscaled.
+__device__ __forceinline__ void accum8_pow2(uint4 q, uint64_t gi0, uint64_t keep_lo,
+                                            uint64_t keep_hi, double& acc_s, double& acc_k) {
+    const uint32_t w[4] = {q.x, q.y, q.z, q.w};
+    if (gi0 + 8 > keep_lo && gi0 < keep_hi) {           // rare: straddles the kept range
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const double d = h2d((j & 1) ? hi16(w[j >> 1]) : lo16(w[j >> 1]));
+            if (gi0 + j >= keep_lo && gi0 + j < keep_hi) acc_k = __fma_rn(d, d, acc_k);
+            else acc_s = __fma_rn(d, d, acc_s);
+        }
+        return;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const double d = h2d((j & 1) ? hi16(w[j >> 1]) : lo16(w[j >> 1]));
+        acc_s = __fma_rn(d, d, acc_s);
+    }
+}
+
 __global__ void __launch_bounds__(kThreads) pass1_kernel(StepParams p) {
     __shared__ double s_sum[kThreads / 32];
     __shared__ unsigned long long s_bad[kThreads / 32];
     __shared__ int s_last;
     const float inv = __fdiv_rn(1.0f, p.st->loss_scale);   // training.rs:244
-    double acc = 0.0;
-    unsigned long long bad = 0;
+    const uint32_t ib = __float_as_uint(inv);
+    const bool pow2 = (ib & 0x7FFFFFu) == 0 && (ib & 0x7F800000u) != 0 &&
+                      (ib & 0x7F800000u) != 0x7F800000u;
+    double acc_s = 0.0, acc_k = 0.0;
+    uint32_t amax = 0;
     const uint4* g = reinterpret_cast<const uint4*>(p.g16);
     const uint64_t nvec = p.n >> 3;
     const uint64_t stride = (uint64_t)gridDim.x * kThreads;
@@ -100,21 +140,38 @@ __global__ void __launch_bounds__(kThreads) pass1_kernel(StepParams p) {
         }
 #pragma unroll
         for (int u = 0; u < kUnroll1; ++u) {
+            amax = absmax2(amax, q[u].x);
+            amax = absmax2(amax, q[u].y);
+            amax = absmax2(amax, q[u].z);
+            amax = absmax2(amax, q[u].w);
             const uint64_t i = base + u * stride;
-            if (i < nvec) accum8(q[u], p.offset + (i << 3), inv, p.keep_lo, p.keep_hi, acc, bad);
+            if (i < nvec) {
+                if (pow2) accum8_pow2(q[u], p.offset + (i << 3), p.keep_lo, p.keep_hi, acc_s, acc_k);
+                else accum8_general(q[u], p.offset + (i << 3), inv, p.keep_lo, p.keep_hi, acc_s);
+            }
         }
     }
     // ragged tail (n % 8 elements)
     if (blockIdx.x == 0 && threadIdx.x < (p.n & 7u)) {
         const uint64_t i = (nvec << 3) + threadIdx.x;
         const uint16_t h = p.g16[i];
-        bad += ((h & 0x7C00u) == 0x7C00u);
+        amax = absmax2(amax, h);
         const uint64_t gi = p.offset + i;
-        const float f = h2f(h);
-        const float u = (gi >= p.keep_lo && gi < p.keep_hi) ? f : __fmul_rn(f, inv);
-        const double d = (double)u;
-        acc = __fma_rn(d, d, acc);
+        const bool keep = gi >= p.keep_lo && gi < p.keep_hi;
+        if (pow2) {
+            const double d = h2d(h);
+            if (keep) acc_k = __fma_rn(d, d, acc_k);
+            else acc_s = __fma_rn(d, d, acc_s);
+        } else {
+            const float f = h2f(h);
+            const double d = (double)(keep ? f : __fmul_rn(f, inv));
+            acc_s = __fma_rn(d, d, acc_s);
+        }
     }
+    // fold the power-of-two scaling in per thread (exact): sum of u^2
+    const double inv_d = (double)inv;
+    const double acc = pow2 ? __fma_rn(acc_s, inv_d * inv_d, acc_k) : acc_s;
+    const unsigned long long bad = ((amax & 0xFFFFu) >= 0x7C00u) || ((amax >> 16) >= 0x7C00u);
     const double bsum = block_sum<kThreads>(acc, s_sum);
     const unsigned long long bbad = block_sum_u64<kThreads>(bad, s_bad);
     if (threadIdx.x == 0) {
@@ -133,7 +190,7 @@ __global__ void __launch_bounds__(kThreads) pass1_kernel(StepParams p) {
     b = block_sum_u64<kThreads>(b, s_bad);
     if (threadIdx.x == 0) {
         p.part_local->sumsq = a;
-        p.part_local->nonfinite = b;
+        p.part_local->nonfinite = b;   // threads that saw an inf/NaN (> 0 iff any)
     }
 }
 

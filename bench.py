@@ -66,8 +66,9 @@ def pass2_traffic_per_param():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled every 200 ms while running."""
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    """nvidia-smi clocks and throttle reasons sampled every 50 ms; summary()
+    keeps the samples taken inside the timed window [t0, t1]."""
+    Q = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
@@ -75,6 +76,7 @@ class ClockSampler:
         self.gpu = gpu_index
         self.proc = None
         self.path = None
+        self.t0 = self.t1 = None
 
     def __enter__(self):
         fd, self.path = tempfile.mkstemp(prefix="ark_clocks_", suffix=".csv")
@@ -82,14 +84,19 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.Q}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            time.sleep(1.0)           # let the sampler start before the timed region
         except OSError:
             self.proc = None
         return self
 
+    def mark(self, which):
+        setattr(self, which, time.time())
+
     def __exit__(self, *a):
         if self.proc:
+            time.sleep(0.2)
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
@@ -97,23 +104,37 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self):
+        import datetime
         if not self.proc or not self.path:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         rows = []
         for line in open(self.path):
             parts = [p.strip() for p in line.split(",")]
-            if len(parts) >= 9:
-                rows.append(parts)
+            if len(parts) < 10:
+                continue
+            try:
+                ts = datetime.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                rows.append((ts, float(parts[2]), float(parts[3]), parts[6:10], parts[4]))
+            except ValueError:
+                continue
         os.unlink(self.path)
-        if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        inside = [r for r in rows if self.t0 and self.t0 <= r[0] <= self.t1]
+        widened = False
+        if not inside and rows and self.t0:
+            # window shorter than the sampling period: nearest samples around it
+            inside = [r for r in rows if self.t0 - 0.25 <= r[0] <= self.t1 + 0.25]
+            widened = True
+        if not inside:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"],
+                    "samples": 0}
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i] == "Active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
-                "samples": len(rows)}
+        reasons = sorted({names[i] for r in inside for i in range(4) if r[3][i] == "Active"})
+        out = {"sm_mhz": statistics.median(r[1] for r in inside),
+               "sm_max_mhz": max(r[2] for r in inside), "reasons": reasons,
+               "samples": len(inside)}
+        if widened:
+            out["window"] = "timed region shorter than the 50 ms sampling period; +-250 ms"
+        return out
 
 
 def cpu_reference_step_setup(L, threads):
@@ -215,7 +236,7 @@ def run_ours(args):
     if world > 1:
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-    L = layout.eko_layout()
+    L = layout.flat_layout(args.params) if args.params else layout.eko_layout()
     comm = adist.nccl_comm(rank, world, local) if world > 1 else None
     adam = ab.AdamConfig(**EKO_HPARAMS)
     scale = ab.LossScaleConfig(init=LOSS_SCALE, every=2000, max=2.0 ** 24)
@@ -238,28 +259,30 @@ def run_ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
-    for _ in range(args.warmup):
-        opt.step_all(w16, g16, m, v)
-    torch.cuda.synchronize()
-
     # ---- timed region: K steps, kernel events recorded by the library ----
-    if not args.graph:
-        opt.profile_begin(args.steps)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
+        for _ in range(args.warmup):
+            opt.step_all(w16, g16, m, v)
+        torch.cuda.synchronize()
+        if not args.graph:
+            opt.profile_begin(args.steps)
         barrier()
         torch.cuda.synchronize()
+        clocks.mark("t0")
         ev0.record(stream)
         for _ in range(args.steps):
             opt.step_all(w16, g16, m, v)
         ev1.record(stream)
         torch.cuda.synchronize()
+        clocks.mark("t1")
         barrier()
     step_ms_local = ev0.elapsed_time(ev1) / args.steps
     prof = None if args.graph else opt.profile_read(args.steps)
     step_ms = max_over_ranks(step_ms_local)
     st = opt.status()
     assert st["last_overflow"] == 0 and st["opt_step"] == START_STEP - 1 + args.warmup + args.steps
+    e2e_steps = min(args.steps, 50)
 
     # ---- e2e: host grads -> device, step, status back, every step ----
     g_host = torch.empty(n, dtype=torch.float16, pin_memory=True)
@@ -268,14 +291,14 @@ def run_ours(args):
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
-    for _ in range(args.steps):
+    for _ in range(e2e_steps):
         opt.upload_grads(g16, g_host)
         opt.step_all(w16, g16, m, v)
         opt.status()
     e1.record(stream)
     torch.cuda.synchronize()
     barrier()
-    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps)
 
     # ---- roofline of the dominant kernel (pass 2) ----
     peak, peak_src = measured_peak()
@@ -300,7 +323,7 @@ def run_ours(args):
     geom = opt.geometry()
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and not args.params:
         cpu = cpu_baseline_single_thread(L)
 
     if rank == 0:
@@ -312,7 +335,9 @@ def run_ours(args):
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded splitmix64 + Irwin-Hall normals with the BASELINE "
                     "distributions, generated on the device)",
-            "config": {"workload": "EKO-237M full optimizer step (BASELINE configs[0])",
+            "config": {"workload": ("EKO-237M full optimizer step (BASELINE configs[0])"
+                                    if not args.params else
+                                    f"flat buffer of {L.n} params (BASELINE configs[4])"),
                        "params": L.n, "params_per_gpu": n, "tensors": L.n_tensors,
                        "parallelism": f"zero1-dp{world}", "t": START_STEP,
                        "loss_scale": LOSS_SCALE, "clip": "active",
@@ -324,6 +349,7 @@ def run_ours(args):
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_val, 2), "unit": "GB/s", "ms_per_step": round(e2e_ms, 3),
                     "h2d_bytes_per_step": 2 * L.n, "d2h_bytes_per_step": 64 * world,
+                    "steps": e2e_steps,
                     "path": "Optimizer.upload_grads (pinned host fp16 grads) + step_all + "
                             "status() per step, through the C ABI"},
             "gpu_launches": 2 * args.steps,
@@ -340,8 +366,10 @@ def run_ours(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
-    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--params", type=int, default=0,
+                    help="flat-buffer workload of this many params instead of EKO-237M")
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--graph", action="store_true", help="replay the step as a CUDA graph")
     ap.add_argument("--no-cpu-baseline", action="store_true")

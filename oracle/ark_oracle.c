@@ -175,14 +175,16 @@ ORK_API void ork_adam_step_f32(float* w, const float* g, float* m, float* v, uin
 typedef struct { double s, c; } ork_acc;
 static inline void acc_add(ork_acc* a, double x) {
     double t = a->s + x;
+    if (!isfinite(t)) { a->s = t; return; }      /* inf/NaN: the plain sum is the answer */
     if (fabs(a->s) >= fabs(x)) a->c += (a->s - t) + x; else a->c += (x - t) + a->s;
     a->s = t;
 }
+static inline double acc_value(const ork_acc* a) { return isfinite(a->s) ? a->s + a->c : a->s; }
 
 ORK_API double ork_sumsq_f32_exact(const float* g, uint64_t n) {
     ork_acc a = {0.0, 0.0};
     for (uint64_t i = 0; i < n; ++i) { double x = (double)g[i]; acc_add(&a, x * x); }
-    return a.s + a.c;
+    return acc_value(&a);
 }
 
 /* The norm expression used by every accurate path: round the exact sum to
@@ -275,7 +277,7 @@ ORK_API void ork_partial_f16(const ork_step_cfg* cfg, const ork_amp_state* st,
         double d = (double)u;
         acc_add(&a, d * d);
     }
-    *sumsq = a.s + a.c;
+    *sumsq = acc_value(&a);
     *nonfinite = bad;
 }
 
