@@ -137,22 +137,27 @@ class ClockSampler:
         return out
 
 
-def cpu_reference_step_setup(L, threads):
-    """The reference's own CPU path (per-tensor, FP32 grads) on this host."""
+def cpu_reference_step_setup(L, threads, n_tensors=None):
+    """The reference's own CPU path (per tensor, FP32 grads) on this host,
+    over the first n_tensors tensors of the reference order (all by
+    default)."""
     from oracle import oracle
-    n = L.n
+    k = L.n_tensors if n_tensors is None else n_tensors
+    tensors = L.tensors[:k]
+    n = sum(t.numel for t in tensors)
     w16 = oracle.synth_f16(n, 0, SEED, 1, 0.02)
     g32 = oracle.dequant(oracle.synth_f16(n, 0, SEED, 2, 1e-3, LOSS_SCALE))
     m = oracle.synth_f32(n, 0, SEED, 3, 1e-4)
     v = oracle.synth_f32(n, 0, SEED, 4, 1e-3, square=True)
     g_fresh = g32.copy()
-    ts = (oracle.Tensor * L.n_tensors)()
-    # reference order (optimizer.rs:185-227) over views into the flat arrays
-    for i, t in enumerate(L.tensors):
-        o = L.offsets[t.name]
+    ts = (oracle.Tensor * k)()
+    o = 0
+    # reference order (optimizer.rs:185-227), contiguous host arrays as in memory.rs
+    for i, t in enumerate(tensors):
         ts[i] = oracle.Tensor(w16[o:].ctypes.data, g32[o:].ctypes.data, m[o:].ctypes.data,
                               v[o:].ctypes.data, t.numel, EKO_HPARAMS["weight_decay"] if t.decay
                               else 0.0, 0 if t.name == "gamma_final" else 1)
+        o += t.numel
     st = oracle.make_state(LOSS_SCALE, opt_step=START_STEP - 1)
     keep = (w16, g32, m, v, g_fresh)
 
@@ -160,13 +165,35 @@ def cpu_reference_step_setup(L, threads):
         np.copyto(g32, g_fresh)           # fresh grads each step (the backward's job; untimed)
         t0 = time.perf_counter()
         rc = oracle.lib().ork_ref_step_tensors(
-            ts, L.n_tensors, st, EKO_HPARAMS["lr"], EKO_HPARAMS["beta1"], EKO_HPARAMS["beta2"],
+            ts, k, st, EKO_HPARAMS["lr"], EKO_HPARAMS["beta1"], EKO_HPARAMS["beta2"],
             EKO_HPARAMS["eps"], EKO_HPARAMS["grad_clip"], 2.0 ** 24, 2000, threads)
         dt = time.perf_counter() - t0
         assert rc == 0
         return dt
 
-    return step, keep
+    step.n_params = n
+    step.n_tensors = k
+    step.keep = keep
+    return step
+
+
+def bounded_reference_step(L, threads, n_steps, budget_s):
+    """A full-EKO step if n_steps of them fit in budget_s, else the longest
+    prefix of the reference tensor order that does (a bounded sample)."""
+    full = cpu_reference_step_setup(L, threads)
+    t_full = min(full(), full())
+    per_step = budget_s / max(n_steps, 1)
+    if t_full <= per_step:
+        return full, t_full
+    target = L.n * per_step / t_full
+    acc, k = 0, 0
+    for t in L.tensors:
+        if k > 0 and acc + t.numel > target:
+            break
+        acc += t.numel
+        k += 1
+    del full
+    return cpu_reference_step_setup(L, threads, k), t_full
 
 
 def run_reference(args):
@@ -181,34 +208,37 @@ def run_reference(args):
     oracle.build()
     threads = oracle.lib().ork_max_threads()
     L = layout.eko_layout()
-    step, _keep = cpu_reference_step_setup(L, threads)
+    step, t_full = bounded_reference_step(L, threads, args.steps + args.warmup, budget_s=150.0)
     for _ in range(args.warmup):
         step()
     times = [step() for _ in range(args.steps)]
     t = statistics.mean(times)
-    value = BYTES_PER_PARAM * L.n / t / 1e9
+    value = BYTES_PER_PARAM * step.n_params / t / 1e9
+    sample = (f"full EKO-237M step ({L.n} params, {L.n_tensors} tensors)" if step.n_tensors ==
+              L.n_tensors else
+              f"first {step.n_tensors} of {L.n_tensors} tensors in reference order "
+              f"({step.n_params} params) per step; full step measured at {t_full * 1e3:.1f} ms")
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(t * 1e3, 3), "higher_is_better": True, "scaling": "strong",
+        "ms_per_step": round(t * 1e3 * L.n / step.n_params, 3), "higher_is_better": True,
+        "scaling": "strong",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, BASELINE distributions)",
         "config": {"workload": "EKO-237M full optimizer step (BASELINE configs[0])",
                    "params": L.n, "tensors": L.n_tensors, "grads": "fp32 (reference layout)"},
         "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads,
-                         "kind": "port",
-                         "sample": f"full EKO-237M step x {args.steps} (all {L.n} params, "
-                                   f"{L.n_tensors} tensors)"},
+                         "kind": "port", "sample": sample},
         "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
 
 
-def cpu_baseline_single_thread(L, budget_s=15.0):
+def cpu_baseline_single_thread(L, budget_s=20.0):
     """1-thread reference path (faithful to the reference's single thread)."""
     from oracle import oracle
     oracle.build()
-    step, _keep = cpu_reference_step_setup(L, 1)
+    step = cpu_reference_step_setup(L, 1)
     times = []
     t_end = time.perf_counter() + budget_s
     while not times or (time.perf_counter() < t_end and len(times) < 3):
