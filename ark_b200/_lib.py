@@ -64,6 +64,7 @@ SIGNATURES = {
     "ark_asm_grad_clip": (c_f, [c_p, c_u64, c_f]),
     "ark_quant_f32_to_f16": (None, [c_p, c_p, c_u64]),
     "ark_dequant_f16_to_f32": (None, [c_p, c_p, c_u64]),
+    "ark_cuda_grad_clip_noalloc": (c_i, [c_p, c_u64, c_f, c_p, c_p]),
     "ark_cuda_last_error": (c_i, []),
     "ark_cuda_strerror": (ctypes.c_char_p, [c_i]),
     "ark_cuda_set_compat": (c_i, [c_u32]),

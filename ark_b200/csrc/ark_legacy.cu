@@ -372,6 +372,72 @@ static int clip_launch(float* g, uint64_t n, float thr, float* norm_out) {
     return ARK_OK;
 }
 
+// ------------------------------------------------------------ grad clip, no allocation
+// Scratch of ark_cuda_grad_clip_noalloc, in the module image instead of a
+// cudaMalloc'd buffer: bytes [0, 256) hold the last-block ticket, [256, 512)
+// the {norm, scale, apply} result, then one double partial per thread block.
+// Every GPU that loads this library holds these 16.5 KiB until the process
+// exits.  All calls share it.
+constexpr int kNoAllocMaxBlocks = 2048;
+constexpr size_t kNoAllocScratchBytes = 512 + sizeof(double) * kNoAllocMaxBlocks;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+static std::mutex g_noalloc_mu;
+static void* g_noalloc_addr[64];   // device address of g_noalloc_scratch, per device
+
+// Set-up, once per device, with that device current: the host-side name of a
+// __device__ array is only a stand-in, so its device address is looked up.
+static int noalloc_scratch(int dev, ClipScratch* sc) {
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (!g_noalloc_addr[dev]) {
+        void* p = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (e != cudaSuccess) {
+            fprintf(stderr, "[ark_cuda] ark_cuda_grad_clip_noalloc: cudaGetSymbolAddress: %s\n",
+                    cudaGetErrorString(e));
+            return ARK_E_CUDA;
+        }
+        g_noalloc_addr[dev] = p;
+    }
+    char* b = static_cast<char*>(g_noalloc_addr[dev]);
+    sc->ticket = reinterpret_cast<unsigned int*>(b);
+    sc->res = reinterpret_cast<ClipResult*>(b + 256);
+    sc->blk = reinterpret_cast<double*>(b + 512);
+    return ARK_OK;
+}
+
+static int clip_noalloc_launch(float* g, uint64_t n, float thr, float* norm_dev,
+                               cudaStream_t s) {
+    if (!norm_dev || (n && !g)) return ARK_E_INVALID_ARG;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return ARK_E_NO_DEVICE;
+    ClipScratch sc;
+    int rc = noalloc_scratch(dev, &sc);
+    if (rc) return rc;
+    if (n == 0)   // empty: norm 0, nothing to scale (as ark_asm_grad_clip)
+        return cudaMemsetAsync(norm_dev, 0, sizeof(float), s) == cudaSuccess ? ARK_OK : ARK_E_CUDA;
+    // the same grid as ark_asm_grad_clip, so both reduce in the same order
+    const int blocks = streaming_grid(reinterpret_cast<const void*>(clip_norm_kernel), kT, 0,
+                                      (n >> 2) + 1);
+    if (blocks > kNoAllocMaxBlocks) {
+        fprintf(stderr,
+                "[ark_cuda] ark_cuda_grad_clip_noalloc: needs %d block partials, the static "
+                "scratch holds %d\n", blocks, kNoAllocMaxBlocks);
+        return ARK_E_UNSUPPORTED;
+    }
+    // the ticket must start at zero; a call that stopped early could have left it set
+    if (cudaMemsetAsync(sc.ticket, 0, sizeof(unsigned int), s) != cudaSuccess) return ARK_E_CUDA;
+    clip_norm_kernel<<<blocks, kT, 0, s>>>(g, n, thr, sc);
+    const int sblocks = streaming_grid(reinterpret_cast<const void*>(clip_scale_kernel), kT, 0,
+                                       (n >> 2) + 1);
+    clip_scale_kernel<<<sblocks, kT, 0, s>>>(g, n, sc.res);
+    if (cudaGetLastError() != cudaSuccess) return ARK_E_CUDA;
+    if (cudaMemcpyAsync(norm_dev, &sc.res->norm, sizeof(float), cudaMemcpyDeviceToDevice, s) !=
+        cudaSuccess)
+        return ARK_E_CUDA;
+    return ARK_OK;
+}
+
 // ------------------------------------------------------------ conversions
 __global__ void __launch_bounds__(kT) quant_kernel(const float* __restrict__ src,
                                                   uint16_t* __restrict__ dst, uint64_t n, int vec) {
@@ -476,6 +542,12 @@ void ark_quant_f32_to_f16(const float* src, uint16_t* dst, uint64_t n) {
 void ark_dequant_f16_to_f32(const uint16_t* src, float* dst, uint64_t n) {
     const int rc = convert_launch(src, dst, n, false);
     if (rc) legacy_fail("ark_dequant_f16_to_f32", rc, nullptr); else set_last_error(ARK_OK);
+}
+
+int ark_cuda_grad_clip_noalloc(float* grads, uint64_t n, float threshold, float* norm_out,
+                               void* cuda_stream) {
+    return clip_noalloc_launch(grads, n, threshold, norm_out,
+                               reinterpret_cast<cudaStream_t>(cuda_stream));
 }
 
 int ark_cuda_last_error(void) { return t_last_error; }

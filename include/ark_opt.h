@@ -80,6 +80,25 @@ ARK_API void ark_quant_f32_to_f16(const float* src, uint16_t* dst, uint64_t n);
  * exact widening. */
 ARK_API void ark_dequant_f16_to_f32(const uint16_t* src, float* dst, uint64_t n);
 
+/* No counterpart in the reference.  The same clip as ark_asm_grad_clip
+ * (same kernels, same grid, same result), for callers that cannot allocate
+ * device memory: a process whose HBM is taken up front by its own pool
+ * allocator, where a cudaMalloc of even a few KiB fails, and code paths
+ * that must not stall other work on the device, which cudaFree does.
+ * ark_asm_grad_clip allocates its scratch on first use; this entry point
+ * calls no cudaMalloc, cudaFree or allocating routine.  Its scratch is a
+ * static 16.5 KiB array in the library's device image (one per GPU that
+ * loads the library, held until exit) with room for 2048 thread-block
+ * partial sums; a launch that needs more is rejected with
+ * ARK_E_UNSUPPORTED.  grads: device, scaled in place; norm_out: a device
+ * float that receives the pre-clip norm; enqueued on cuda_stream (NULL:
+ * the default stream), nothing is waited for.  The first call on a device
+ * looks up the array's device address (cudaGetSymbolAddress); make that
+ * first call before any stream capture.  All calls share the array:
+ * calls that overlap on the GPU (other streams, other threads) race. */
+ARK_API int ark_cuda_grad_clip_noalloc(float* grads, uint64_t n, float threshold,
+                                       float* norm_out, void* cuda_stream);
+
 /* ---- controls for the legacy entry points (no reference counterpart;
  *      the reference has no error channel and no streams) ------------- */
 #define ARK_COMPAT_CLIP_NEON_FOLD  0x1u  /* ark_asm_grad_clip: reference f32 fold */
