@@ -72,8 +72,8 @@ class ClockSampler:
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index):
-        self.gpu = gpu_index
+    def __init__(self, gpu_ids):
+        self.gpu = ",".join(gpu_ids)
         self.proc = None
         self.path = None
         self.t0 = self.t1 = None
@@ -135,6 +135,19 @@ class ClockSampler:
         if widened:
             out["window"] = "timed region shorter than the 50 ms sampling period; +-250 ms"
         return out
+
+
+def nvidia_smi_ids(devices):
+    """nvidia-smi ids (UUIDs) of CUDA devices: nvidia-smi numbers GPUs
+    physically and ignores CUDA_VISIBLE_DEVICES."""
+    import torch
+    out = []
+    for d in devices:
+        try:
+            out.append("GPU-" + str(torch.cuda.get_device_properties(d).uuid))
+        except Exception:
+            out.append(str(d))
+    return out
 
 
 def cpu_reference_step_setup(L, threads, n_tensors=None):
@@ -206,7 +219,8 @@ def run_reference(args):
     from ark_b200 import layout
     from oracle import oracle
     oracle.build()
-    threads = oracle.lib().ork_max_threads()
+    # every host core this process may run on (torchrun sets OMP_NUM_THREADS=1)
+    threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
     L = layout.eko_layout()
     step, t_full = bounded_reference_step(L, threads, args.steps + args.warmup, budget_s=150.0)
     for _ in range(args.warmup):
@@ -291,7 +305,8 @@ def run_ours(args):
 
     # ---- timed region: K steps, kernel events recorded by the library ----
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks:
+    sampled = list(range(world)) if rank == 0 else [local]
+    with ClockSampler(nvidia_smi_ids(sampled)) as clocks:
         for _ in range(args.warmup):
             opt.step_all(w16, g16, m, v)
         torch.cuda.synchronize()

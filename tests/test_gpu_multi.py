@@ -1,0 +1,123 @@
+"""The ZeRO-1 sharded step on 2 GPUs (one process per GPU, the library's
+NCCL communicator for the 16-byte exchange) against the CPU oracle run on
+the whole buffer: every rank's shard bit for bit, the replicated loss-scale
+state identical on every rank, and the FP16 weight all-gather.  Skipped
+when fewer than 2 GPUs are visible."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+WORLD = 2
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _rank_main(rank, world, port, q):
+    import datetime
+
+    import torch.distributed as dist
+
+    import ark_b200 as ab
+    from ark_b200 import dist as adist
+    from ark_b200 import layout, synth
+    from oracle import oracle
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    comm = None
+    try:
+        comm = adist.nccl_comm(rank, world, rank)
+        L = layout.decoder_layout("multi", 4, 96, 256, 1000)
+        seed, scale = 77, 65536.0
+        adam = ab.AdamConfig(lr=3e-4, beta1=0.9, beta2=0.95, eps=1e-8, weight_decay=0.1,
+                             grad_clip=1.0)
+        sc = ab.LossScaleConfig(init=scale, every=3, max=2.0 ** 24)
+        opt = ab.Optimizer(L, adam, sc, device=rank, rank=rank, world=world, comm=comm,
+                           constant_lr=True, initial_step=999)
+        lo, hi, n = opt.lo, opt.hi, opt.n
+        w16, g16, m, v = synth.make_state(n, lo, seed, "cuda", loss_scale=scale)
+        inject_step = 3
+        statuses = []
+        for k in range(1, 6):
+            if k == inject_step:
+                idx = int(oracle.lib().ork_inject_index(seed, k, L.n))
+                if lo <= idx < hi:
+                    g16.view(torch.int16)[idx - lo] = 0x7C00
+            if k == inject_step + 1:
+                synth.fill_grads(g16, lo, seed, scale)        # clean grads again
+            opt.step_all(w16, g16, m, v)
+            statuses.append(opt.status())
+        stride = -(-L.n // world) + 128
+        full = torch.zeros(stride * world, dtype=torch.float16, device="cuda")
+        shard = torch.zeros(stride, dtype=torch.float16, device="cuda")
+        shard[:n] = w16
+        opt.allgather_weights(shard, full, stride)
+        torch.cuda.synchronize()
+        q.put((rank, lo, hi, w16.cpu().numpy().view(np.uint16), m.cpu().numpy(),
+               v.cpu().numpy(), statuses, full.cpu().numpy().view(np.uint16), stride))
+        opt.close()
+    finally:
+        if comm:
+            adist.nccl_comm_destroy(comm)
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason="needs 2 GPUs")
+def test_two_gpu_zero1_step_matches_oracle(oracle):
+    from ark_b200 import layout, synth
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_rank_main, args=(r, WORLD, port, q)) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    res = sorted([q.get(timeout=300) for _ in range(WORLD)], key=lambda r: r[0])
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    # oracle on the whole buffer, same schedule
+    L = layout.decoder_layout("multi", 4, 96, 256, 1000)
+    seed, scale, n = 77, 65536.0, L.n
+    w = oracle.synth_f16(n, 0, seed, synth.STREAM_W, 0.02)
+    g = oracle.synth_f16(n, 0, seed, synth.STREAM_G, 1e-3, scale)
+    g_clean = g.copy()
+    m = oracle.synth_f32(n, 0, seed, synth.STREAM_M, 1e-4)
+    v = oracle.synth_f32(n, 0, seed, synth.STREAM_V, 1e-3, square=True)
+    cfg = oracle.make_cfg(n_decay=L.n_decay, scale_every=3, scale_max=2.0 ** 24)
+    st = oracle.make_state(scale, opt_step=999)
+    ref_states = []
+    for k in range(1, 6):
+        if k == 3:
+            g[oracle.lib().ork_inject_index(seed, k, n)] = 0x7C00
+        if k == 4:
+            g = g_clean.copy()
+        s, bad = oracle.partial_f16(cfg, st, g, 0)
+        oracle.apply_f16(cfg, st, w, g, m, v, 0, s, bad)
+        ref_states.append((st.loss_scale, st.opt_step, st.last_overflow, st.clean_steps,
+                           st.last_norm))
+    for rank, lo, hi, ws, ms, vs, sts, full, stride in res:
+        assert np.array_equal(ws, w[lo:hi]), rank
+        assert np.array_equal(ms.view(np.uint32), m[lo:hi].view(np.uint32)), rank
+        assert np.array_equal(vs.view(np.uint32), v[lo:hi].view(np.uint32)), rank
+        got = [(s["loss_scale"], s["opt_step"], s["last_overflow"], s["clean_steps"],
+                s["last_norm"]) for s in sts]
+        for a, b in zip(got, ref_states):
+            assert a[:4] == b[:4]
+            assert abs(a[4] - b[4]) <= 1e-5 * max(b[4], 1e-30)
+        for r2, lo2, hi2, *_ in res:                      # all-gathered weights
+            assert np.array_equal(full[r2 * stride: r2 * stride + (hi2 - lo2)], w[lo2:hi2])
+    assert res[0][6][-1] == res[1][6][-1]                 # replicated state identical
