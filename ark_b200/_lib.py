@@ -13,7 +13,7 @@ PKG = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(PKG)
 LIB_PATH = os.path.join(PKG, "lib", "libark_cuda.so")
 
-ARK_OPT_ABI_VERSION = 1
+ARK_OPT_ABI_VERSION = 2
 ARK_OK = 0
 STATUS_NAMES = {
     0: "ARK_OK", -1: "ARK_E_INVALID_ARG", -2: "ARK_E_MISALIGNED", -3: "ARK_E_CUDA",
@@ -24,6 +24,7 @@ ARK_E_EARLY_STOP = -6
 ARK_COMPAT_CLIP_NEON_FOLD = 0x1
 ARK_OPT_COMPAT_GAMMA_FINAL_UNSCALED = 0x1
 ARK_OPT_USE_GRAPH = 0x2
+ARK_OPT_TWO_PASS = 0x4
 
 c_f, c_u32, c_u64, c_i, c_i32, c_d, c_p = (ctypes.c_float, ctypes.c_uint32, ctypes.c_uint64,
                                            ctypes.c_int, ctypes.c_int32, ctypes.c_double,
@@ -40,7 +41,7 @@ class OptCfg(ctypes.Structure):
         ("scale_init", c_f), ("scale_backoff", c_f), ("scale_growth", c_f), ("scale_min", c_f),
         ("scale_max", c_f), ("scale_every", c_u32), ("max_consecutive_nans", c_u32),
         ("initial_step", c_u32), ("flags", c_u32), ("rank", c_i32), ("world_size", c_i32),
-        ("nccl_comm", c_p), ("stream", c_p),
+        ("nccl_comm", c_p), ("stream", c_p), ("wait_timeout_ms", c_u32), ("reserved", c_u32),
     ]
 
 

@@ -24,6 +24,7 @@
 #include <vector>
 
 #include "ark_device.cuh"
+#include "ark_fused.cuh"
 #include "ark_internal.h"
 
 namespace ark {
@@ -200,21 +201,18 @@ struct Plan {
     float inv, s, norm, lr;
     double sumsq;
     uint32_t t;
-    int skip;       // overflow or early stop: no element work
+    int skip;       // overflow, early stop or error: no element work
     int clip;
     int overflow;
+    int error;      // ARK_E_* raised while forming the plan (0 = none)
 };
 
-__device__ void make_plan(const StepParams& p, Plan& pl) {
-    const ark_opt_status st = *p.st;
-    double sumsq = 0.0;
-    unsigned long long bad = 0;
-    for (int r = 0; r < p.world; ++r) {               // rank order: deterministic
-        sumsq += p.part_all[r].sumsq;
-        bad += p.part_all[r].nonfinite;
-    }
+// The step plan from the device state and the global {sum, non-finite}.
+__device__ void make_plan_from(const ark_opt_status& st, double sumsq, unsigned long long bad,
+                               const StepParams& p, Plan& pl) {
     pl.sumsq = sumsq;
     pl.overflow = bad != 0;
+    pl.error = 0;
     pl.skip = pl.overflow || st.early_stop;
     pl.inv = __fdiv_rn(1.0f, st.loss_scale);          // training.rs:244
     pl.t = st.opt_step + 1u;                          // optimizer.rs:172
@@ -226,12 +224,24 @@ __device__ void make_plan(const StepParams& p, Plan& pl) {
     pl.k = adam_scalars(pl.lr, p.beta1, p.beta2, p.eps, p.wd, pl.t);
 }
 
+__device__ void make_plan(const StepParams& p, Plan& pl) {
+    const ark_opt_status st = *p.st;
+    double sumsq = 0.0;
+    unsigned long long bad = 0;
+    for (int r = 0; r < p.world; ++r) {               // rank order: deterministic
+        sumsq += p.part_all[r].sumsq;
+        bad += p.part_all[r].nonfinite;
+    }
+    make_plan_from(st, sumsq, bad, p, pl);
+}
+
 // State machine update (training.rs:293-305 on overflow, :316-326 after a
 // clean step); runs once per step in the last pass-2 block.
 __device__ void advance_state(const StepParams& p, const Plan& pl) {
     ark_opt_status st = *p.st;
     st.steps_called += 1;
-    if (st.early_stop) {
+    if (pl.error) st.error = pl.error;
+    if (st.early_stop || pl.error) {
         *p.st = st;
         return;
     }
@@ -353,6 +363,370 @@ __global__ void __launch_bounds__(kThreads) pass2_kernel(StepParams p, uint16_t*
     if (threadIdx.x == 0) advance_state(p, pl);
 }
 
+// ======================================================================
+// The persistent single-kernel step (default when cooperative launch is
+// available): every CTA of a co-resident grid owns a contiguous range of
+// 2048-element tiles.  Phase 1 streams its gradients through a 4-stage
+// shared-memory ring filled by 1-D bulk copies (TMA engine); a grid barrier
+// (last-arriving CTA) reduces the CTA partials in a fixed order, exchanges
+// the 16-byte rank partials with the peers over NVLink (P2P stores into
+// their receive slots, world > 1) and publishes the plan; phase 2 walks the
+// same tiles in reverse, so the gradient tiles read last in phase 1 are
+// still in L2, with g, w, m, v brought in by bulk copies and w, m, v
+// written back with streaming stores.  Every wait is bounded by the global
+// timer; a timeout turns the step into a no-op and raises ARK_E_TIMEOUT in
+// the device state.
+// ======================================================================
+constexpr int kFT = 256;                       // threads per CTA
+constexpr int kStages = 4;
+constexpr int kTile2Vec = kFT;                 // phase-2 tile: 256 x 8 = 2048 elements
+constexpr int kTile1Vec = 4 * kFT;             // phase-1 tile: 1024 x 8 = 8192 elements (16 KB)
+constexpr int kStage2Bytes = kTile2Vec * 8 * 12;   // g 4 KB | w 4 KB | m 8 KB | v 8 KB
+constexpr int kStage1Bytes = kTile1Vec * 16;
+constexpr int kFusedSmem = kStages * kStage2Bytes; // 96 KB, phase 1 uses the first 64 KB
+constexpr int kMaxP2PRanks = 32;
+static_assert(kStages * kStage1Bytes <= kFusedSmem, "phase-1 ring fits");
+
+struct FusedParams {
+    uint16_t* w16;
+    float* m;
+    float* v;
+    Plan* plan;                     // published by the last CTA of phase 1
+    uint64_t* release;              // == epoch once the plan is published
+    unsigned int* arrive;           // phase-1 arrival counter
+    unsigned int* err;              // CTA-local failures (bulk-copy wait timeouts)
+    uint64_t* xchg;                 // this rank's receive slots [2][world][4] x u64
+    uint64_t* const* peers;         // receive-slot bases of every rank (peers[rank] == xchg)
+    int rank;
+    int keep_g_in_l2;               // phase-1 gradient loads with L2 evict_last
+    uint64_t local_timeout_ns, peer_timeout_ns;
+};
+
+// 4 elements of phase 2 (one half of a thread's 8): same arithmetic as update8.
+__device__ __forceinline__ void update4(uint2& wq, const uint2 gq, float4& mm, float4& vv,
+                                        uint64_t gi0, const Plan& pl, const StepParams& p) {
+    const uint32_t gw[2] = {gq.x, gq.y};
+    const uint32_t ww[2] = {wq.x, wq.y};
+    float mv[4] = {mm.x, mm.y, mm.z, mm.w};
+    float vv4[4] = {vv.x, vv.y, vv.z, vv.w};
+    const bool keep_any = (gi0 + 4 > p.keep_lo) && (gi0 < p.keep_hi);
+    const bool dec_all = gi0 + 4 <= p.n_decay;
+    const bool dec_none = gi0 >= p.n_decay;
+    uint16_t wout[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const uint16_t gh = (j & 1) ? hi16(gw[j >> 1]) : lo16(gw[j >> 1]);
+        const uint16_t wh = (j & 1) ? hi16(ww[j >> 1]) : lo16(ww[j >> 1]);
+        float gf = h2f(gh);
+        const bool keep = keep_any && (gi0 + j >= p.keep_lo) && (gi0 + j < p.keep_hi);
+        if (!keep) gf = __fmul_rn(gf, pl.inv);                       // training.rs:308
+        if (pl.clip) gf = __fmul_rn(gf, pl.s);                       // optimizer.rs:151-166
+        const bool dec = dec_all || (!dec_none && gi0 + j < p.n_decay);
+        const float decay = dec ? pl.k.decay : 1.0f;
+        wout[j] = f2h(adam_elem(h2f(wh), gf, mv[j], vv4[j], pl.k, decay));
+    }
+    wq = make_uint2(pack16(wout[0], wout[1]), pack16(wout[2], wout[3]));
+    mm = make_float4(mv[0], mv[1], mv[2], mv[3]);
+    vv = make_float4(vv4[0], vv4[1], vv4[2], vv4[3]);
+}
+
+__device__ __forceinline__ void copy_plan_from_global(Plan& dst, const Plan* src) {
+    static_assert(sizeof(Plan) % 4 == 0, "plan words");
+    const unsigned int* s = reinterpret_cast<const unsigned int*>(src);
+    unsigned int* d = reinterpret_cast<unsigned int*>(&dst);
+#pragma unroll
+    for (int i = 0; i < (int)(sizeof(Plan) / 4); ++i) d[i] = __ldcg(s + i);
+}
+
+__global__ void __launch_bounds__(kFT) fused_step_kernel(StepParams p, FusedParams f) {
+    extern __shared__ __align__(128) unsigned char ring[];
+    __shared__ __align__(8) uint64_t bar1[kStages];
+    __shared__ __align__(8) uint64_t bar2[kStages];
+    __shared__ double s_sum[kFT / 32];
+    __shared__ unsigned long long s_bad[kFT / 32];
+    __shared__ double s_rsum[kMaxP2PRanks];
+    __shared__ unsigned long long s_rbad[kMaxP2PRanks];
+    __shared__ int s_rok[kMaxP2PRanks];
+    __shared__ Plan s_plan;
+    __shared__ int s_flag, s_err;
+    const int tid = threadIdx.x;
+    // Step sequence number; the state is only advanced after every CTA has
+    // passed the final ticket, so all CTAs read the same value here.
+    const unsigned long long epoch = p.st->steps_called + 1ull;
+    if (tid == 0) {
+        for (int i = 0; i < kStages; ++i) {
+            mbar_init(&bar1[i], 1);
+            mbar_init(&bar2[i], 1);
+        }
+        fence_barrier_init();
+        s_err = 0;
+    }
+    __syncthreads();
+
+    const uint64_t nvec = p.n >> 3;
+    const uint64_t ntiles = (nvec + kTile2Vec - 1) / kTile2Vec;
+    const uint64_t t_lo = ntiles * blockIdx.x / gridDim.x;
+    const uint64_t t_hi = ntiles * (blockIdx.x + 1) / gridDim.x;
+    const uint64_t v_lo = t_lo * kTile2Vec;
+    const uint64_t v_hi = t_hi * kTile2Vec < nvec ? t_hi * kTile2Vec : nvec;
+
+    // ------------------------------------------------ phase 1
+    const float inv = __fdiv_rn(1.0f, p.st->loss_scale);   // training.rs:244
+    const uint32_t ib = __float_as_uint(inv);
+    const bool pow2 = (ib & 0x7FFFFFu) == 0 && (ib & 0x7F800000u) != 0 &&
+                      (ib & 0x7F800000u) != 0x7F800000u;
+    double acc_s = 0.0, acc_k = 0.0;
+    uint32_t amax = 0;
+    {
+        const uint64_t pol = f.keep_g_in_l2 ? policy_evict_last() : policy_evict_first();
+        const int n1 = v_hi > v_lo ? (int)((v_hi - v_lo + kTile1Vec - 1) / kTile1Vec) : 0;
+        int issued = 0, done = 0;
+        auto issue = [&](int k) {
+            const uint64_t a = v_lo + (uint64_t)k * kTile1Vec;
+            const uint32_t cnt = (uint32_t)(v_hi - a < (uint64_t)kTile1Vec ? v_hi - a : kTile1Vec);
+            const int st = k % kStages;
+            mbar_arrive_expect_tx(&bar1[st], cnt * 16u);
+            bulk_load(ring + st * kStage1Bytes, p.g16 + a * 8, cnt * 16u, &bar1[st], pol);
+        };
+        if (tid == 0)
+            for (; issued < kStages - 1 && issued < n1; ++issued) issue(issued);
+        for (int k = 0; k < n1; ++k) {
+            if (tid == 0 && issued < n1) issue(issued++);
+            const int st = k % kStages;
+            if (!mbar_wait(&bar1[st], (uint32_t)(k / kStages) & 1u, f.local_timeout_ns)) s_err = 1;
+            __syncthreads();
+            if (s_err) break;
+            done = k + 1;
+            const uint64_t a = v_lo + (uint64_t)k * kTile1Vec;
+            const uint32_t cnt = (uint32_t)(v_hi - a < (uint64_t)kTile1Vec ? v_hi - a : kTile1Vec);
+            const uint4* tile = reinterpret_cast<const uint4*>(ring + st * kStage1Bytes);
+            for (uint32_t j = tid; j < cnt; j += kFT) {
+                const uint4 q = tile[j];
+                amax = absmax2(amax, q.x);
+                amax = absmax2(amax, q.y);
+                amax = absmax2(amax, q.z);
+                amax = absmax2(amax, q.w);
+                const uint64_t gi0 = p.offset + ((a + j) << 3);
+                if (pow2) accum8_pow2(q, gi0, p.keep_lo, p.keep_hi, acc_s, acc_k);
+                else accum8_general(q, gi0, inv, p.keep_lo, p.keep_hi, acc_s);
+            }
+            __syncthreads();   // the stage may be refilled
+        }
+        if (s_err && tid == 0) {
+            // drain copies still in flight into this CTA's ring before it is reused or left
+            for (int k = done; k < issued; ++k)
+                mbar_wait(&bar1[k % kStages], (uint32_t)(k / kStages) & 1u, f.local_timeout_ns);
+            atomicExch(f.err, (unsigned int)ARK_E_TIMEOUT);
+        }
+    }
+    if (blockIdx.x == 0 && tid < (p.n & 7u)) {          // ragged tail (n % 8)
+        const uint64_t i = (nvec << 3) + tid;
+        const uint16_t h = p.g16[i];
+        amax = absmax2(amax, h);
+        const uint64_t gi = p.offset + i;
+        const bool keep = gi >= p.keep_lo && gi < p.keep_hi;
+        if (pow2) {
+            const double d = h2d(h);
+            if (keep) acc_k = __fma_rn(d, d, acc_k);
+            else acc_s = __fma_rn(d, d, acc_s);
+        } else {
+            const float fl = h2f(h);
+            const double d = (double)(keep ? fl : __fmul_rn(fl, inv));
+            acc_s = __fma_rn(d, d, acc_s);
+        }
+    }
+    {
+        const double inv_d = (double)inv;
+        const double acc = pow2 ? __fma_rn(acc_s, inv_d * inv_d, acc_k) : acc_s;
+        const unsigned long long bad = ((amax & 0xFFFFu) >= 0x7C00u) || ((amax >> 16) >= 0x7C00u);
+        const double bsum = block_sum<kFT>(acc, s_sum);
+        const unsigned long long bbad = block_sum_u64<kFT>(bad, s_bad);
+        if (tid == 0) {
+            p.blk_sum[blockIdx.x] = bsum;
+            p.blk_bad[blockIdx.x] = bbad;
+        }
+    }
+    // ------------------------------------------------ grid barrier + exchange
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) s_flag = atomicAdd(f.arrive, 1u) == gridDim.x - 1;
+    __syncthreads();
+    if (s_flag) {
+        __threadfence();
+        double a = 0.0;
+        unsigned long long b = 0;
+        for (unsigned int i = tid; i < gridDim.x; i += kFT) {
+            a += __ldcg(p.blk_sum + i);
+            b += __ldcg(p.blk_bad + i);
+        }
+        a = block_sum<kFT>(a, s_sum);
+        b = block_sum_u64<kFT>(b, s_bad);
+        if (tid == 0) {
+            *f.arrive = 0u;   // re-armed for the next step
+            s_sum[0] = a;     // broadcast this rank's partial
+            s_bad[0] = b;
+        }
+        __syncthreads();
+        if (tid < kMaxP2PRanks) {
+            const int r = tid;
+            double rs = 0.0;
+            unsigned long long rb = 0;
+            int ok = 1;
+            if (p.world == 1) {
+                if (r == 0) {
+                    rs = s_sum[0];
+                    rb = s_bad[0];
+                }
+            } else if (r < p.world) {
+                // my partial -> rank r's slot [epoch & 1][my rank], payload before epoch
+                uint64_t* dst = f.peers[r] + (((epoch & 1ull) * p.world + f.rank) * 4);
+                st_relaxed_sys_v2(dst, (uint64_t)__double_as_longlong(s_sum[0]), s_bad[0]);
+                st_release_sys(dst + 2, epoch);
+                // rank r's partial <- my slot [epoch & 1][r]
+                const uint64_t* src = f.xchg + (((epoch & 1ull) * p.world + r) * 4);
+                const uint64_t t0 = global_ns();
+                while (ld_acquire_sys(src + 2) != epoch) {
+                    if (global_ns() - t0 > f.peer_timeout_ns) {
+                        ok = 0;
+                        break;
+                    }
+                    __nanosleep(32);
+                }
+                if (ok) {
+                    uint64_t x, y;
+                    ld_relaxed_sys_v2(src, x, y);
+                    rs = __longlong_as_double((long long)x);
+                    rb = y;
+                }
+            }
+            s_rsum[r] = rs;
+            s_rbad[r] = rb;
+            s_rok[r] = ok;
+        }
+        __syncthreads();
+        if (tid == 0) {
+            double sum = 0.0;
+            unsigned long long bad = 0;
+            int ok = 1;
+            for (int r = 0; r < p.world; ++r) {           // rank order: deterministic
+                sum += s_rsum[r];
+                bad += s_rbad[r];
+                ok &= s_rok[r];
+            }
+            Plan pl;
+            const ark_opt_status st = *p.st;
+            make_plan_from(st, sum, bad, p, pl);
+            const unsigned int e = atomicAdd(f.err, 0u);
+            if (!ok || e) {
+                pl.skip = 1;
+                pl.error = ARK_E_TIMEOUT;
+            }
+            *f.plan = pl;
+            __threadfence();
+            st_release_gpu(f.release, epoch);
+        }
+    }
+    if (tid == 0) {
+        const uint64_t t0 = global_ns();
+        const uint64_t limit = f.peer_timeout_ns + f.local_timeout_ns;
+        bool ok = true;
+        while (ld_acquire_gpu(f.release) != epoch) {
+            if (global_ns() - t0 > limit) {
+                ok = false;
+                break;
+            }
+            __nanosleep(64);
+        }
+        if (ok) {
+            copy_plan_from_global(s_plan, f.plan);
+        } else {
+            s_plan.skip = 1;
+            s_plan.error = ARK_E_TIMEOUT;
+            s_plan.overflow = 0;
+        }
+    }
+    __syncthreads();
+    const Plan pl = s_plan;
+
+    // ------------------------------------------------ phase 2 (reverse tile order)
+    if (!pl.skip) {
+        const uint64_t pol_g = policy_evict_first();
+        const uint64_t pol_s = policy_evict_first();
+        const int n2 = (int)(t_hi - t_lo);
+        int issued = 0, done = 0;
+        auto tile_of = [&](int k) { return t_hi - 1 - (uint64_t)k; };
+        auto issue = [&](int k) {
+            const uint64_t a = tile_of(k) * kTile2Vec;
+            const uint32_t cnt = (uint32_t)(nvec - a < (uint64_t)kTile2Vec ? nvec - a : kTile2Vec);
+            const int st = k % kStages;
+            unsigned char* base = ring + st * kStage2Bytes;
+            mbar_arrive_expect_tx(&bar2[st], cnt * 96u);
+            bulk_load(base, p.g16 + a * 8, cnt * 16u, &bar2[st], pol_g);
+            bulk_load(base + 4096, f.w16 + a * 8, cnt * 16u, &bar2[st], pol_s);
+            bulk_load(base + 8192, f.m + a * 8, cnt * 32u, &bar2[st], pol_s);
+            bulk_load(base + 16384, f.v + a * 8, cnt * 32u, &bar2[st], pol_s);
+        };
+        if (tid == 0)
+            for (; issued < kStages - 1 && issued < n2; ++issued) issue(issued);
+        for (int k = 0; k < n2; ++k) {
+            if (tid == 0 && issued < n2) issue(issued++);
+            const int st = k % kStages;
+            if (!mbar_wait(&bar2[st], (uint32_t)(k / kStages) & 1u, f.local_timeout_ns)) s_err = 1;
+            __syncthreads();
+            if (s_err) break;
+            done = k + 1;
+            const uint64_t a = tile_of(k) * kTile2Vec;
+            const uint32_t nel = (uint32_t)((nvec - a < (uint64_t)kTile2Vec ? nvec - a : kTile2Vec) * 8);
+            const unsigned char* base = ring + st * kStage2Bytes;
+            const uint2* gs = reinterpret_cast<const uint2*>(base);
+            const uint2* ws = reinterpret_cast<const uint2*>(base + 4096);
+            const float4* ms = reinterpret_cast<const float4*>(base + 8192);
+            const float4* vs = reinterpret_cast<const float4*>(base + 16384);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const uint32_t q = (uint32_t)tid + h * kFT;   // 4-element group within the tile
+                if (q * 4 < nel) {
+                    uint2 wq = ws[q];
+                    float4 mm = ms[q], vv = vs[q];
+                    const uint64_t e0 = a * 8 + (uint64_t)q * 4;   // shard element index
+                    update4(wq, gs[q], mm, vv, p.offset + e0, pl, p);
+                    __stcs(reinterpret_cast<uint2*>(f.w16 + e0), wq);
+                    __stcs(reinterpret_cast<float4*>(f.m + e0), mm);
+                    __stcs(reinterpret_cast<float4*>(f.v + e0), vv);
+                }
+            }
+            __syncthreads();
+        }
+        if (s_err && tid == 0) {
+            for (int k = done; k < issued; ++k)
+                mbar_wait(&bar2[k % kStages], (uint32_t)(k / kStages) & 1u, f.local_timeout_ns);
+            atomicExch(f.err, (unsigned int)ARK_E_TIMEOUT);
+        }
+        if (blockIdx.x == 0 && tid < (p.n & 7u)) {       // ragged tail
+            const uint64_t i = (nvec << 3) + tid;
+            const uint64_t gi = p.offset + i;
+            float gf = h2f(p.g16[i]);
+            if (!(gi >= p.keep_lo && gi < p.keep_hi)) gf = __fmul_rn(gf, pl.inv);
+            if (pl.clip) gf = __fmul_rn(gf, pl.s);
+            const float decay = gi < p.n_decay ? pl.k.decay : 1.0f;
+            float mi = f.m[i], vi = f.v[i];
+            f.w16[i] = f2h(adam_elem(h2f(f.w16[i]), gf, mi, vi, pl.k, decay));
+            f.m[i] = mi;
+            f.v[i] = vi;
+        }
+    }
+    // ------------------------------------------------ state machine
+    if (!last_block_arrived(p.ticket2, &s_flag)) return;
+    if (tid == 0) {
+        Plan fin = pl;
+        const unsigned int e = atomicExch(f.err, 0u);
+        if (e && !fin.error) {
+            fin.error = (int)e;
+        }
+        advance_state(p, fin);
+    }
+}
+
 }  // namespace ark
 
 // ======================================================================
@@ -376,6 +750,19 @@ struct ark_opt_state {
     Partial* d_part_all = nullptr;
     ark_opt_status* h_status = nullptr;  // pinned
     int blocks1 = 0, blocks2 = 0;
+    // persistent single-kernel step
+    bool fused = false;
+    int fused_blocks = 0;
+    Plan* d_plan = nullptr;
+    uint64_t* d_release = nullptr;
+    unsigned int* d_arrive = nullptr;
+    unsigned int* d_err = nullptr;
+    // P2P exchange slots (world > 1)
+    bool p2p = false;
+    uint64_t* xchg = nullptr;                 // own receive slots (cudaMalloc, IPC-exported)
+    std::vector<uint64_t*> peer_slots;        // every rank's slots, mapped here
+    uint64_t** d_peers = nullptr;             // device copy of peer_slots
+    uint64_t timeout_ns = 0;
     // graph replay
     cudaGraphExec_t graph = nullptr;
     cudaStream_t capture_stream = nullptr;
@@ -396,7 +783,95 @@ int check_cfg(const ark_opt_cfg* c) {
         return ARK_E_INVALID_ARG;
     if (c->scale_every == 0) return ARK_E_INVALID_ARG;
     if (c->keep_scaled_hi < c->keep_scaled_lo) return ARK_E_INVALID_ARG;
+    if (c->flags & ~(ARK_OPT_COMPAT_GAMMA_FINAL_UNSCALED | ARK_OPT_USE_GRAPH | ARK_OPT_TWO_PASS))
+        return ARK_E_INVALID_ARG;
     return ARK_OK;
+}
+
+FusedParams make_fused(const ark_opt_state* s, uint16_t* w16, float* m, float* v) {
+    FusedParams f;
+    f.w16 = w16;
+    f.m = m;
+    f.v = v;
+    f.plan = s->d_plan;
+    f.release = s->d_release;
+    f.arrive = s->d_arrive;
+    f.err = s->d_err;
+    f.xchg = s->xchg;
+    f.peers = s->d_peers;
+    f.rank = s->cfg.rank;
+    // keep the shard's gradients in L2 between the phases when they fit comfortably
+    f.keep_g_in_l2 = s->cfg.n * 2 <= (uint64_t)64 << 20;
+    f.local_timeout_ns = 2000000000ull;
+    f.peer_timeout_ns = s->timeout_ns;
+    return f;
+}
+
+// Exchange-slot set-up for the fused step on world > 1: each rank exports
+// its receive slots through CUDA IPC, the handles are all-gathered over the
+// rank's NCCL communicator, and every rank maps its peers' slots.  All ranks
+// then agree (NCCL min-reduction) whether every mapping succeeded; if not,
+// every rank uses the two-kernel step with the NCCL exchange instead.
+int setup_p2p(ark_opt_state* s) {
+    const int W = s->cfg.world_size, R = s->cfg.rank;
+    if (W < 2 || W > kMaxP2PRanks || !s->comm) return ARK_OK;
+    const size_t slot_bytes = sizeof(uint64_t) * 4 * 2 * (size_t)W;
+    int ok = 1;
+    char* d_tmp = nullptr;   // [W] handles | ok flag
+    if (cudaMalloc(&s->xchg, slot_bytes) != cudaSuccess) ok = 0;
+    if (ok && cudaMemset(s->xchg, 0, slot_bytes) != cudaSuccess) ok = 0;
+    cudaIpcMemHandle_t mine;
+    memset(&mine, 0, sizeof(mine));
+    if (ok && cudaIpcGetMemHandle(&mine, s->xchg) != cudaSuccess) ok = 0;
+    const size_t hb = sizeof(cudaIpcMemHandle_t);
+    if (cudaMalloc(&d_tmp, hb * W + 256) != cudaSuccess) return ARK_E_CUDA;
+    int* d_ok = reinterpret_cast<int*>(d_tmp + hb * W);
+    std::vector<cudaIpcMemHandle_t> all(W);
+    cudaMemcpy(d_tmp + hb * R, &mine, hb, cudaMemcpyHostToDevice);
+    if (ncclAllGather(d_tmp + hb * R, d_tmp, hb, ncclUint8, s->comm, s->stream) != ncclSuccess)
+        return ARK_E_NCCL;
+    if (cudaStreamSynchronize(s->stream) != cudaSuccess) return ARK_E_CUDA;
+    cudaMemcpy(all.data(), d_tmp, hb * W, cudaMemcpyDeviceToHost);
+    s->peer_slots.assign(W, nullptr);
+    for (int r = 0; r < W && ok; ++r) {
+        if (r == R) {
+            s->peer_slots[r] = s->xchg;
+            continue;
+        }
+        void* p = nullptr;
+        if (cudaIpcOpenMemHandle(&p, all[r], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
+            cudaGetLastError();
+            ok = 0;
+            break;
+        }
+        s->peer_slots[r] = static_cast<uint64_t*>(p);
+    }
+    if (ok) {
+        if (cudaMalloc(&s->d_peers, sizeof(uint64_t*) * W) != cudaSuccess ||
+            cudaMemcpy(s->d_peers, s->peer_slots.data(), sizeof(uint64_t*) * W,
+                       cudaMemcpyHostToDevice) != cudaSuccess)
+            ok = 0;
+    }
+    cudaMemcpy(d_ok, &ok, sizeof(int), cudaMemcpyHostToDevice);
+    if (ncclAllReduce(d_ok, d_ok, 1, ncclInt32, ncclMin, s->comm, s->stream) != ncclSuccess)
+        return ARK_E_NCCL;
+    if (cudaStreamSynchronize(s->stream) != cudaSuccess) return ARK_E_CUDA;
+    int all_ok = 0;
+    cudaMemcpy(&all_ok, d_ok, sizeof(int), cudaMemcpyDeviceToHost);
+    cudaFree(d_tmp);
+    s->p2p = all_ok != 0;
+    return ARK_OK;
+}
+
+void teardown_p2p(ark_opt_state* s) {
+    for (size_t r = 0; r < s->peer_slots.size(); ++r)
+        if (s->peer_slots[r] && s->peer_slots[r] != s->xchg) cudaIpcCloseMemHandle(s->peer_slots[r]);
+    s->peer_slots.clear();
+    if (s->d_peers) cudaFree(s->d_peers);
+    if (s->xchg) cudaFree(s->xchg);
+    s->d_peers = nullptr;
+    s->xchg = nullptr;
+    s->p2p = false;
 }
 
 StepParams make_params(const ark_opt_state* s, const uint16_t* g16) {
@@ -438,6 +913,27 @@ int enqueue_step(ark_opt_state* s, cudaStream_t stream, uint16_t* w16, const uin
     StepParams p = make_params(s, g16);
     cudaEvent_t* ev = nullptr;
     if (profile) ev = &s->prof_events[4 * s->prof_used];
+    if (s->fused) {
+        FusedParams f = make_fused(s, w16, m, v);
+        cudaLaunchConfig_t lc;
+        memset(&lc, 0, sizeof(lc));
+        lc.gridDim = dim3((unsigned)s->fused_blocks);
+        lc.blockDim = dim3(kFT);
+        lc.dynamicSmemBytes = kFusedSmem;
+        lc.stream = stream;
+        cudaLaunchAttribute attr[1];
+        attr[0].id = cudaLaunchAttributeCooperative;   // all CTAs co-resident (grid barrier)
+        attr[0].val.cooperative = 1;
+        lc.attrs = attr;
+        lc.numAttrs = 1;
+        if (ev) ARK_CUDA_TRY(cudaEventRecord(ev[2], stream));
+        ARK_CUDA_TRY(cudaLaunchKernelEx(&lc, fused_step_kernel, p, f));
+        if (ev) {
+            ARK_CUDA_TRY(cudaEventRecord(ev[3], stream));
+            s->prof_used++;
+        }
+        return ARK_OK;
+    }
     if (ev) ARK_CUDA_TRY(cudaEventRecord(ev[0], stream));
     pass1_kernel<<<s->blocks1, kThreads, 0, stream>>>(p);
     ARK_CUDA_TRY(cudaGetLastError());
@@ -498,6 +994,22 @@ int ark_cuda_opt_init(const ark_opt_cfg* cfg, ark_opt_state** out) {
     s->blocks2 = streaming_grid(reinterpret_cast<const void*>(pass2_kernel), kThreads, 0,
                                 (cfg->n >> 3) / kUnroll2 + 1);
     const int W = cfg->world_size;
+    s->timeout_ns = (uint64_t)(cfg->wait_timeout_ms ? cfg->wait_timeout_ms : 5000u) * 1000000ull;
+    // persistent single-kernel step: every SM filled with co-resident CTAs
+    int coop = 0, sms = 0, per_sm = 0;
+    cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, cfg->device);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, cfg->device);
+    if (coop && !(cfg->flags & ARK_OPT_TWO_PASS) && W <= kMaxP2PRanks &&
+        cudaFuncSetAttribute(fused_step_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kFusedSmem) == cudaSuccess &&
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fused_step_kernel, kFT,
+                                                      kFusedSmem) == cudaSuccess &&
+        per_sm > 0) {
+        s->fused = true;
+        s->fused_blocks = sms * per_sm;
+    }
+    cudaGetLastError();
+    const int nblk = s->blocks1 > s->fused_blocks ? s->blocks1 : s->fused_blocks;
     // carve one allocation: state | lr table | block partials | tickets | partials
     size_t off = 0;
     auto take = [&](size_t bytes) {
@@ -507,11 +1019,13 @@ int ark_cuda_opt_init(const ark_opt_cfg* cfg, ark_opt_state** out) {
     };
     const size_t o_state = take(sizeof(ark_opt_status));
     const size_t o_lr = take(sizeof(float) * cfg->lr_table_len);
-    const size_t o_bs = take(sizeof(double) * s->blocks1);
-    const size_t o_bb = take(sizeof(unsigned long long) * s->blocks1);
-    const size_t o_tk = take(sizeof(unsigned int) * 2);
+    const size_t o_bs = take(sizeof(double) * nblk);
+    const size_t o_bb = take(sizeof(unsigned long long) * nblk);
+    const size_t o_tk = take(sizeof(unsigned int) * 4);
     const size_t o_pl = take(sizeof(Partial));
     const size_t o_pa = take(sizeof(Partial) * W);
+    const size_t o_plan = take(sizeof(Plan));
+    const size_t o_rel = take(sizeof(uint64_t));
     if (cudaMalloc(&s->dmem, off) != cudaSuccess) {
         ark_cuda_opt_destroy(s);
         return ARK_E_CUDA;
@@ -524,6 +1038,10 @@ int ark_cuda_opt_init(const ark_opt_cfg* cfg, ark_opt_state** out) {
     s->d_tickets = reinterpret_cast<unsigned int*>(base + o_tk);
     s->d_part_local = reinterpret_cast<Partial*>(base + o_pl);
     s->d_part_all = reinterpret_cast<Partial*>(base + o_pa);
+    s->d_arrive = s->d_tickets + 2;
+    s->d_err = s->d_tickets + 3;
+    s->d_plan = reinterpret_cast<Plan*>(base + o_plan);
+    s->d_release = reinterpret_cast<uint64_t*>(base + o_rel);
     // single-GPU: pass 1 writes the rank partial straight into the gathered slot
     if (W == 1) s->d_part_local = s->d_part_all;
     if (cudaMallocHost(&s->h_status, sizeof(ark_opt_status)) != cudaSuccess) {
@@ -546,6 +1064,17 @@ int ark_cuda_opt_init(const ark_opt_cfg* cfg, ark_opt_state** out) {
         return ARK_E_CUDA;
     }
     s->cfg.lr_table = nullptr;  // host table not retained
+    if (W > 1 && s->fused) {
+        rc = setup_p2p(s);
+        if (rc) {
+            ark_cuda_opt_destroy(s);
+            return rc;
+        }
+        if (!s->p2p) {            // every rank agreed to fall back
+            teardown_p2p(s);
+            s->fused = false;
+        }
+    }
     *out = s;
     return ARK_OK;
 }
@@ -661,6 +1190,8 @@ int ark_cuda_opt_profile_read(ark_opt_state* s, float* out, uint32_t capacity, u
         ARK_CUDA_TRY(cudaEventElapsedTime(&out[3 * i + 1], ev[1], ev[2]));
         ARK_CUDA_TRY(cudaEventElapsedTime(&out[3 * i + 2], ev[2], ev[3]));
     }
+    if (s->fused)
+        for (uint32_t i = 0; i < k; ++i) out[3 * i] = out[3 * i + 1] = 0.0f;
     *steps = k;
     s->prof_cap = 0;
     s->prof_used = 0;
@@ -669,9 +1200,9 @@ int ark_cuda_opt_profile_read(ark_opt_state* s, float* out, uint32_t capacity, u
 
 int ark_cuda_opt_geometry(ark_opt_state* s, uint32_t* b1, uint32_t* b2, uint32_t* threads) {
     if (!s) return ARK_E_INVALID_ARG;
-    if (b1) *b1 = (uint32_t)s->blocks1;
-    if (b2) *b2 = (uint32_t)s->blocks2;
-    if (threads) *threads = (uint32_t)kThreads;
+    if (b1) *b1 = s->fused ? 0u : (uint32_t)s->blocks1;
+    if (b2) *b2 = s->fused ? (uint32_t)s->fused_blocks : (uint32_t)s->blocks2;
+    if (threads) *threads = (uint32_t)(s->fused ? kFT : kThreads);
     return ARK_OK;
 }
 
@@ -681,6 +1212,7 @@ int ark_cuda_opt_destroy(ark_opt_state* s) {
     cudaStreamSynchronize(s->stream);
     if (s->graph) cudaGraphExecDestroy(s->graph);
     if (s->capture_stream) cudaStreamDestroy(s->capture_stream);
+    teardown_p2p(s);
     for (cudaEvent_t e : s->prof_events) cudaEventDestroy(e);
     if (s->dmem) cudaFree(s->dmem);
     if (s->h_status) cudaFreeHost(s->h_status);

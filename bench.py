@@ -52,10 +52,10 @@ def measured_peak():
         return 6650.0, "fallback 6.65 TB/s (MEASURED_PEAKS.json absent)"
 
 
-def pass2_traffic_per_param():
-    """DRAM bytes per parameter of the pass-2 kernel from the committed ncu
-    summary (profiles/pass2_adamw_eko.md, line 'dram_bytes_per_param: X')."""
-    p = os.path.join(ROOT, "profiles", "pass2_adamw_eko.md")
+def kernel_traffic_per_param(summary):
+    """DRAM bytes per parameter of a kernel from its committed ncu summary
+    (profiles/<summary>, line 'dram_bytes_per_param: X')."""
+    p = os.path.join(ROOT, "profiles", summary)
     try:
         for line in open(p):
             if line.strip().startswith("dram_bytes_per_param:"):
@@ -287,7 +287,7 @@ def run_ours(args):
     stream = torch.cuda.current_stream(dev)
     opt = ab.Optimizer(L, adam, scale, device=local, rank=rank, world=world, comm=comm,
                        stream=stream, constant_lr=True, initial_step=START_STEP - 1,
-                       use_graph=args.graph)
+                       use_graph=args.graph, two_pass=args.two_pass)
     lo, n = opt.lo, opt.n
     w16, g16, m, v = synth.make_state(n, lo, SEED, dev, loss_scale=LOSS_SCALE)
     torch.cuda.synchronize()
@@ -348,13 +348,26 @@ def run_ours(args):
     # ---- roofline of the dominant kernel (pass 2) ----
     peak, peak_src = measured_peak()
     roof = None
-    if prof is not None and len(prof):
+    if prof is not None and len(prof) and opt.fused:
+        k_ms = float(np.mean(prof[:, 2]))
+        k_max = max_over_ranks(k_ms)
+        achieved = BYTES_PER_PARAM * n / (k_ms * 1e-3) / 1e9
+        tpp = kernel_traffic_per_param("fused_step_eko.md")
+        roof = {"kernel": "ark::fused_step_kernel (finite check + norm + exchange + unscale + "
+                          "clip + AdamW + loss-scale state, one persistent kernel)",
+                "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "peak_source": peak_src,
+                "traffic": round(tpp * n) if tpp else None,
+                "algorithmic_bytes_per_launch": BYTES_PER_PARAM * n,
+                "kernel_ms": round(k_ms, 4), "kernel_ms_max_rank": round(k_max, 4),
+                "launches_per_step": 1}
+    elif prof is not None and len(prof):
         p1 = float(np.mean(prof[:, 0]))
         ex = float(np.mean(prof[:, 1]))
         p2 = float(np.mean(prof[:, 2]))
         p2_max = max_over_ranks(p2)
         achieved = PASS2_BYTES_PER_PARAM * n / (p2 * 1e-3) / 1e9
-        tpp = pass2_traffic_per_param()
+        tpp = kernel_traffic_per_param("pass2_adamw_eko.md")
         roof = {"kernel": "ark::pass2_kernel (fused unscale+clip+AdamW)", "bound": "hbm",
                 "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "peak_source": peak_src,
@@ -363,7 +376,7 @@ def run_ours(args):
                 "pass2_ms": round(p2, 4), "pass2_ms_max_rank": round(p2_max, 4),
                 "pass1_ms": round(p1, 4),
                 "pass1_gbs": round(PASS1_BYTES_PER_PARAM * n / (p1 * 1e-3) / 1e9, 1),
-                "exchange_ms": round(ex, 4)}
+                "exchange_ms": round(ex, 4), "launches_per_step": 2}
     clk = clocks.summary()
     geom = opt.geometry()
 
@@ -387,6 +400,7 @@ def run_ours(args):
                        "parallelism": f"zero1-dp{world}", "t": START_STEP,
                        "loss_scale": LOSS_SCALE, "clip": "active",
                        "bytes_per_param": BYTES_PER_PARAM, "graph": bool(args.graph),
+                       "step_kernel": "persistent single kernel" if opt.fused else "two kernels",
                        "l2": "inputs larger than L2 (state %.2f GB/GPU vs 126 MB L2); no flush"
                              % (n * 12 / 1e9),
                        "geometry": geom},
@@ -397,7 +411,7 @@ def run_ours(args):
                     "steps": e2e_steps,
                     "path": "Optimizer.upload_grads (pinned host fp16 grads) + step_all + "
                             "status() per step, through the C ABI"},
-            "gpu_launches": 2 * args.steps,
+            "gpu_launches": (1 if opt.fused else 2) * args.steps,
             "clocks": clk,
         }
         print(json.dumps(line), flush=True)
@@ -417,6 +431,8 @@ def main():
                     help="flat-buffer workload of this many params instead of EKO-237M")
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--graph", action="store_true", help="replay the step as a CUDA graph")
+    ap.add_argument("--two-pass", action="store_true",
+                    help="two kernels per step instead of the persistent single kernel")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:

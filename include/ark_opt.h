@@ -25,7 +25,7 @@
 extern "C" {
 #endif
 
-#define ARK_OPT_ABI_VERSION 1u
+#define ARK_OPT_ABI_VERSION 2u
 
 /* ---- status codes (0 = success; negative = error) --------------------- */
 #define ARK_OK               0
@@ -136,6 +136,11 @@ ARK_API uint32_t    ark_cuda_abi_version(void);
 /* Capture the step (pass 1, exchange, pass 2) in a CUDA graph on first use
  * with a given buffer set and replay it afterwards. */
 #define ARK_OPT_USE_GRAPH                   0x2u
+/* Use two kernels per step (pass 1, exchange, pass 2) instead of the
+ * persistent single-kernel step; with world_size > 1 the exchange is then an
+ * NCCL all-gather.  Chosen automatically when cooperative launch or the
+ * peer-to-peer mapping of the exchange slots is unavailable. */
+#define ARK_OPT_TWO_PASS                    0x4u
 
 typedef struct ark_opt_cfg {
     uint32_t     abi_version;          /* ARK_OPT_ABI_VERSION */
@@ -163,6 +168,10 @@ typedef struct ark_opt_cfg {
     void*        nccl_comm;            /* ncclComm_t, required when world_size > 1 */
     void*        stream;               /* cudaStream_t every step runs on (NULL: the
                                           legacy default stream) */
+    uint32_t     wait_timeout_ms;      /* limit of a device-side wait for a peer's partial
+                                          (0: 5000); past it the step is skipped and the
+                                          state reports ARK_E_TIMEOUT */
+    uint32_t     reserved;
 } ark_opt_cfg;
 
 /* Device-resident state, read back by ark_cuda_opt_read_status. */

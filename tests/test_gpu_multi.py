@@ -121,3 +121,60 @@ def test_two_gpu_zero1_step_matches_oracle(oracle):
         for r2, lo2, hi2, *_ in res:                      # all-gathered weights
             assert np.array_equal(full[r2 * stride: r2 * stride + (hi2 - lo2)], w[lo2:hi2])
     assert res[0][6][-1] == res[1][6][-1]                 # replicated state identical
+
+
+def _timeout_rank_main(rank, world, port, q, go):
+    import datetime
+
+    import torch.distributed as dist
+
+    import ark_b200 as ab
+    from ark_b200 import dist as adist
+    from ark_b200 import layout, synth
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    comm = adist.nccl_comm(rank, world, rank)
+    L = layout.flat_layout(1 << 20)
+    opt = ab.Optimizer(L, rank=rank, world=world, comm=comm, device=rank, constant_lr=True,
+                       wait_timeout_ms=500)
+    bufs = synth.make_state(opt.n, opt.lo, 5, "cuda")
+    opt.step_all(*bufs)                       # one step together
+    rc0, st0 = opt.read_status()
+    dist.barrier()
+    result = None
+    if rank == 0:
+        opt.step_all(*bufs)                   # rank 1 has left: the wait must run out
+        rc1, st1 = opt.read_status()
+        # the context is still usable after the timeout
+        x = torch.ones(1024, device="cuda").sum().item()
+        result = (rc0, st0["opt_step"], rc1, st1["error"], st1["opt_step"], x)
+        go.set()
+    else:
+        go.wait(120)                          # stay alive (slots mapped) until rank 0 is done
+        result = (rc0, st0["opt_step"])
+    q.put((rank, result))
+    opt.close()
+    adist.nccl_comm_destroy(comm)
+    dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason="needs 2 GPUs")
+def test_peer_wait_times_out_when_a_rank_leaves():
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    q, go = ctx.Queue(), ctx.Event()
+    procs = [ctx.Process(target=_timeout_rank_main, args=(r, WORLD, port, q, go))
+             for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=300) for _ in range(WORLD))
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    rc0, step0, rc1, err, step_after, x = res[0]
+    assert rc0 == 0 and step0 == 1 and res[1] == (0, 1)
+    assert rc1 == -5 and err == -5           # ARK_E_TIMEOUT, step skipped
+    assert step_after == 1 and x == 1024.0

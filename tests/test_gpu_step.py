@@ -38,14 +38,15 @@ def check_state(dev_st, ost, where=""):
 
 def run_steps(oracle, L, *, steps, scale0=65536.0, initial_step=0, shard=None, compat=False,
               inject=None, lr_table=(3e-4,), use_graph=False, adam=None, scale_cfg=None,
-              fresh_grads=True, max_nans=200, heavy=False):
+              fresh_grads=True, max_nans=200, heavy=False, two_pass=False):
     adam = adam or ab.AdamConfig(lr=3e-4, beta1=0.9, beta2=0.95, eps=1e-8, weight_decay=0.1,
                                  grad_clip=1.0)
     scale_cfg = scale_cfg or ab.LossScaleConfig(init=scale0, every=50, max=2.0 ** 24,
                                                 max_consecutive_nans=max_nans)
     opt = ab.Optimizer(L, adam, scale_cfg, lr_table=np.asarray(lr_table, np.float32),
                        initial_step=initial_step, shard=shard, compat_gamma_final_unscaled=compat,
-                       use_graph=use_graph)
+                       use_graph=use_graph, two_pass=two_pass)
+    assert opt.fused == (not two_pass)
     lo, n = opt.lo, opt.n
     w, g, m, v = oracle_bufs(oracle, n, lo, SEED, scale0, heavy)
     dw, dg, dm, dv = dev(w), dev(g), dev(m), dev(v)
@@ -85,20 +86,30 @@ def tiny():
     return layout.decoder_layout("tiny", 3, 32, 72, 97)
 
 
-def test_tiny_decoder_multi_step(oracle):
-    st, _ = run_steps(oracle, tiny(), steps=6, inject={3: 0x7E00})
+@pytest.mark.parametrize("two_pass", [False, True])
+def test_tiny_decoder_multi_step(oracle, two_pass):
+    st, _ = run_steps(oracle, tiny(), steps=6, inject={3: 0x7E00}, two_pass=two_pass)
     assert st["opt_step"] == 5 and st["skipped_steps"] == 1
 
 
-def test_compat_gamma_final_unscaled(oracle):
-    st, _ = run_steps(oracle, tiny(), steps=3, compat=True)
+@pytest.mark.parametrize("two_pass", [False, True])
+def test_compat_gamma_final_unscaled(oracle, two_pass):
+    st, _ = run_steps(oracle, tiny(), steps=3, compat=True, two_pass=two_pass)
     assert st["opt_step"] == 3
 
 
-@pytest.mark.parametrize("shard", [(1024, 8231), (0, 7), (128, 128 + 8 * 37)])
-def test_shard_offsets_and_ragged_sizes(oracle, shard):
+@pytest.mark.parametrize("two_pass", [False, True])
+@pytest.mark.parametrize("shard", [(1024, 8231), (0, 7), (128, 128 + 8 * 37), (0, 0)])
+def test_shard_offsets_and_ragged_sizes(oracle, shard, two_pass):
     L = tiny()
-    run_steps(oracle, L, steps=2, shard=shard)
+    run_steps(oracle, L, steps=2, shard=shard, two_pass=two_pass)
+
+
+@pytest.mark.parametrize("n", [2048 * 296 * 3 + 8 * 5 + 3, 2048 * 7 + 8, 17])
+def test_tile_boundaries(oracle, n):
+    """Flat sizes around the persistent kernel's 2048-element tiles and its
+    per-CTA tile ranges, with a ragged tail."""
+    run_steps(oracle, layout.flat_layout(n), steps=2, inject={2: 0x7C00})
 
 
 def test_warmup_lr_table_and_resume_step(oracle):
@@ -124,9 +135,11 @@ def test_early_stop(oracle):
     assert st["consecutive_nans"] == 4 and st["opt_step"] == 0
 
 
-def test_eko_full_step_bit_exact(oracle):
+@pytest.mark.parametrize("two_pass", [False, True])
+def test_eko_full_step_bit_exact(oracle, two_pass):
     """EKO-237M full optimizer step, t = 1000, scale 65536."""
-    st, ost = run_steps(oracle, layout.eko_layout(), steps=1, initial_step=999, fresh_grads=False)
+    st, ost = run_steps(oracle, layout.eko_layout(), steps=1, initial_step=999, fresh_grads=False,
+                        two_pass=two_pass)
     assert st["opt_step"] == 1000 and st["last_clip_coef"] < 1.0
     assert st["last_norm"] == ost.last_norm
 
