@@ -24,7 +24,7 @@ ARK_E_EARLY_STOP = -6
 ARK_COMPAT_CLIP_NEON_FOLD = 0x1
 ARK_OPT_COMPAT_GAMMA_FINAL_UNSCALED = 0x1
 ARK_OPT_USE_GRAPH = 0x2
-ARK_OPT_TWO_PASS = 0x4
+ARK_OPT_NCCL_EXCHANGE = 0x4
 
 c_f, c_u32, c_u64, c_i, c_i32, c_d, c_p = (ctypes.c_float, ctypes.c_uint32, ctypes.c_uint64,
                                            ctypes.c_int, ctypes.c_int32, ctypes.c_double,

@@ -98,7 +98,8 @@ class Optimizer:
     stream:  CUDA stream (torch.cuda.Stream or raw handle) every step runs on;
              default: torch's current stream, so the step is ordered after the
              torch work that produced the gradients.
-    two_pass: force the two-kernel step (default: one persistent kernel).
+    nccl_exchange: world > 1: exchange the partials with an NCCL all-gather
+             instead of peer-to-peer stores from pass 1.
     wait_timeout_ms: limit of the device-side wait for peers' partials.
     """
 
@@ -106,7 +107,7 @@ class Optimizer:
                  scale: LossScaleConfig | None = None, *, device: int = 0, rank: int = 0,
                  world: int = 1, comm=None, stream=None, lr_table=None, constant_lr: bool = False,
                  initial_step: int = 0, compat_gamma_final_unscaled: bool = False,
-                 use_graph: bool = False, shard=None, two_pass: bool = False,
+                 use_graph: bool = False, shard=None, nccl_exchange: bool = False,
                  wait_timeout_ms: int = 0):
         self.layout = layout if isinstance(layout, Layout) else flat_layout(int(layout))
         self.adam = adam or AdamConfig()
@@ -129,8 +130,8 @@ class Optimizer:
             flags |= _lib.ARK_OPT_COMPAT_GAMMA_FINAL_UNSCALED
         if use_graph:
             flags |= _lib.ARK_OPT_USE_GRAPH
-        if two_pass:
-            flags |= _lib.ARK_OPT_TWO_PASS
+        if nccl_exchange:
+            flags |= _lib.ARK_OPT_NCCL_EXCHANGE
         cfg = _lib.OptCfg()
         cfg.abi_version = _lib.ARK_OPT_ABI_VERSION
         cfg.device = device
@@ -224,19 +225,12 @@ class Optimizer:
                    _lib.lib().ark_cuda_opt_profile_begin(self._h, max_steps))
 
     def profile_read(self, capacity: int):
-        """Per step [pass-1 ms, exchange ms, pass-2 ms] from CUDA events; with
-        the single-kernel step the whole kernel is in the third column and
-        the first two are 0."""
+        """Per step [pass-1 ms, exchange ms, pass-2 ms] from CUDA events."""
         buf = (ctypes.c_float * (3 * capacity))()
         k = ctypes.c_uint32()
         _lib.check("ark_cuda_opt_profile_read",
                    _lib.lib().ark_cuda_opt_profile_read(self._h, buf, capacity, ctypes.byref(k)))
         return np.frombuffer(buf, np.float32)[: 3 * k.value].reshape(k.value, 3).copy()
-
-    @property
-    def fused(self) -> bool:
-        """True when each step is the persistent single kernel."""
-        return self.geometry()["pass1_blocks"] == 0
 
     def geometry(self):
         b1, b2, t = ctypes.c_uint32(), ctypes.c_uint32(), ctypes.c_uint32()

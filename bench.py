@@ -287,7 +287,7 @@ def run_ours(args):
     stream = torch.cuda.current_stream(dev)
     opt = ab.Optimizer(L, adam, scale, device=local, rank=rank, world=world, comm=comm,
                        stream=stream, constant_lr=True, initial_step=START_STEP - 1,
-                       use_graph=args.graph, two_pass=args.two_pass)
+                       use_graph=args.graph, nccl_exchange=args.nccl_exchange)
     lo, n = opt.lo, opt.n
     w16, g16, m, v = synth.make_state(n, lo, SEED, dev, loss_scale=LOSS_SCALE)
     torch.cuda.synchronize()
@@ -310,8 +310,7 @@ def run_ours(args):
         for _ in range(args.warmup):
             opt.step_all(w16, g16, m, v)
         torch.cuda.synchronize()
-        if not args.graph:
-            opt.profile_begin(args.steps)
+        opt.profile_begin(args.steps)
         barrier()
         torch.cuda.synchronize()
         clocks.mark("t0")
@@ -323,7 +322,7 @@ def run_ours(args):
         clocks.mark("t1")
         barrier()
     step_ms_local = ev0.elapsed_time(ev1) / args.steps
-    prof = None if args.graph else opt.profile_read(args.steps)
+    prof = opt.profile_read(args.steps)
     step_ms = max_over_ranks(step_ms_local)
     st = opt.status()
     assert st["last_overflow"] == 0 and st["opt_step"] == START_STEP - 1 + args.warmup + args.steps
@@ -348,20 +347,7 @@ def run_ours(args):
     # ---- roofline of the dominant kernel (pass 2) ----
     peak, peak_src = measured_peak()
     roof = None
-    if prof is not None and len(prof) and opt.fused:
-        k_ms = float(np.mean(prof[:, 2]))
-        k_max = max_over_ranks(k_ms)
-        achieved = BYTES_PER_PARAM * n / (k_ms * 1e-3) / 1e9
-        tpp = kernel_traffic_per_param("fused_step_eko.md")
-        roof = {"kernel": "ark::fused_step_kernel (finite check + norm + exchange + unscale + "
-                          "clip + AdamW + loss-scale state, one persistent kernel)",
-                "bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                "frac": round(achieved / peak, 4), "peak_source": peak_src,
-                "traffic": round(tpp * n) if tpp else None,
-                "algorithmic_bytes_per_launch": BYTES_PER_PARAM * n,
-                "kernel_ms": round(k_ms, 4), "kernel_ms_max_rank": round(k_max, 4),
-                "launches_per_step": 1}
-    elif prof is not None and len(prof):
+    if prof is not None and len(prof):
         p1 = float(np.mean(prof[:, 0]))
         ex = float(np.mean(prof[:, 1]))
         p2 = float(np.mean(prof[:, 2]))
@@ -400,7 +386,9 @@ def run_ours(args):
                        "parallelism": f"zero1-dp{world}", "t": START_STEP,
                        "loss_scale": LOSS_SCALE, "clip": "active",
                        "bytes_per_param": BYTES_PER_PARAM, "graph": bool(args.graph),
-                       "step_kernel": "persistent single kernel" if opt.fused else "two kernels",
+                       "exchange": ("none" if world == 1 else
+                                    "nccl all-gather" if args.nccl_exchange else
+                                    "p2p stores from pass 1 (nccl if unmappable)"),
                        "l2": "inputs larger than L2 (state %.2f GB/GPU vs 126 MB L2); no flush"
                              % (n * 12 / 1e9),
                        "geometry": geom},
@@ -411,7 +399,7 @@ def run_ours(args):
                     "steps": e2e_steps,
                     "path": "Optimizer.upload_grads (pinned host fp16 grads) + step_all + "
                             "status() per step, through the C ABI"},
-            "gpu_launches": (1 if opt.fused else 2) * args.steps,
+            "gpu_launches": 2 * args.steps,
             "clocks": clk,
         }
         print(json.dumps(line), flush=True)
@@ -430,9 +418,10 @@ def main():
     ap.add_argument("--params", type=int, default=0,
                     help="flat-buffer workload of this many params instead of EKO-237M")
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--graph", action="store_true", help="replay the step as a CUDA graph")
-    ap.add_argument("--two-pass", action="store_true",
-                    help="two kernels per step instead of the persistent single kernel")
+    ap.add_argument("--no-graph", dest="graph", action="store_false",
+                    help="launch the kernels directly instead of replaying a CUDA graph")
+    ap.add_argument("--nccl-exchange", action="store_true",
+                    help="N > 1: exchange the partials with NCCL instead of peer-to-peer stores")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     if args.warmup < 3:

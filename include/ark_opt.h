@@ -126,7 +126,9 @@ ARK_API uint32_t    ark_cuda_abi_version(void);
  * decay applies to global indices [0, n_decay).
  *
  * Multi-GPU (ZeRO-1): rank r owns a contiguous shard; the only exchange is
- * a 16-byte {sum of squares, non-finite count} per rank over NCCL.
+ * a 16-byte {sum of squares, non-finite count} per rank, written by the last
+ * block of pass 1 straight into the peers' memory over NVLink (or an NCCL
+ * all-gather, see ARK_OPT_NCCL_EXCHANGE).
  * ====================================================================== */
 
 /* Reproduce the reference's unscale omission for the final RMSNorm gain
@@ -136,11 +138,11 @@ ARK_API uint32_t    ark_cuda_abi_version(void);
 /* Capture the step (pass 1, exchange, pass 2) in a CUDA graph on first use
  * with a given buffer set and replay it afterwards. */
 #define ARK_OPT_USE_GRAPH                   0x2u
-/* Use two kernels per step (pass 1, exchange, pass 2) instead of the
- * persistent single-kernel step; with world_size > 1 the exchange is then an
- * NCCL all-gather.  Chosen automatically when cooperative launch or the
- * peer-to-peer mapping of the exchange slots is unavailable. */
-#define ARK_OPT_TWO_PASS                    0x4u
+/* world_size > 1: exchange the 16-byte rank partials with an NCCL
+ * all-gather between the two kernels instead of peer-to-peer stores from
+ * the last block of pass 1 (chosen automatically, on every rank, when a
+ * rank cannot map its peers' exchange slots). */
+#define ARK_OPT_NCCL_EXCHANGE               0x4u
 
 typedef struct ark_opt_cfg {
     uint32_t     abi_version;          /* ARK_OPT_ABI_VERSION */

@@ -1,5 +1,5 @@
 """The ZeRO-1 sharded step on 2 GPUs (one process per GPU, the library's
-NCCL communicator for the 16-byte exchange) against the CPU oracle run on
+peer-to-peer exchange of the 16-byte partials, or NCCL) against the CPU oracle run on
 the whole buffer: every rank's shard bit for bit, the replicated loss-scale
 state identical on every rank, and the FP16 weight all-gather.  Skipped
 when fewer than 2 GPUs are visible."""
@@ -24,7 +24,7 @@ def _free_port():
     return p
 
 
-def _rank_main(rank, world, port, q):
+def _rank_main(rank, world, port, q, nccl_exchange):
     import datetime
 
     import torch.distributed as dist
@@ -47,7 +47,7 @@ def _rank_main(rank, world, port, q):
                              grad_clip=1.0)
         sc = ab.LossScaleConfig(init=scale, every=3, max=2.0 ** 24)
         opt = ab.Optimizer(L, adam, sc, device=rank, rank=rank, world=world, comm=comm,
-                           constant_lr=True, initial_step=999)
+                           constant_lr=True, initial_step=999, nccl_exchange=nccl_exchange)
         lo, hi, n = opt.lo, opt.hi, opt.n
         w16, g16, m, v = synth.make_state(n, lo, seed, "cuda", loss_scale=scale)
         inject_step = 3
@@ -77,12 +77,14 @@ def _rank_main(rank, world, port, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason="needs 2 GPUs")
-def test_two_gpu_zero1_step_matches_oracle(oracle):
+@pytest.mark.parametrize("nccl_exchange", [False, True])
+def test_two_gpu_zero1_step_matches_oracle(oracle, nccl_exchange):
     from ark_b200 import layout, synth
     port = _free_port()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_rank_main, args=(r, WORLD, port, q)) for r in range(WORLD)]
+    procs = [ctx.Process(target=_rank_main, args=(r, WORLD, port, q, nccl_exchange))
+             for r in range(WORLD)]
     for p in procs:
         p.start()
     res = sorted([q.get(timeout=300) for _ in range(WORLD)], key=lambda r: r[0])

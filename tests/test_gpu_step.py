@@ -1,4 +1,4 @@
-"""The fused whole-step API (ark_cuda_opt_*) on a B200 against the CPU
+"""The whole-step API (ark_cuda_opt_*) on a B200 against the CPU
 oracle: finite check, unscale, global norm and clip, AdamW over the flat
 decayed-first layout, and the loss-scale state machine, step by step.
 Flags and scale sequences are compared exactly; the norm within 1e-5
@@ -38,15 +38,14 @@ def check_state(dev_st, ost, where=""):
 
 def run_steps(oracle, L, *, steps, scale0=65536.0, initial_step=0, shard=None, compat=False,
               inject=None, lr_table=(3e-4,), use_graph=False, adam=None, scale_cfg=None,
-              fresh_grads=True, max_nans=200, heavy=False, two_pass=False):
+              fresh_grads=True, max_nans=200, heavy=False):
     adam = adam or ab.AdamConfig(lr=3e-4, beta1=0.9, beta2=0.95, eps=1e-8, weight_decay=0.1,
                                  grad_clip=1.0)
     scale_cfg = scale_cfg or ab.LossScaleConfig(init=scale0, every=50, max=2.0 ** 24,
                                                 max_consecutive_nans=max_nans)
     opt = ab.Optimizer(L, adam, scale_cfg, lr_table=np.asarray(lr_table, np.float32),
                        initial_step=initial_step, shard=shard, compat_gamma_final_unscaled=compat,
-                       use_graph=use_graph, two_pass=two_pass)
-    assert opt.fused == (not two_pass)
+                       use_graph=use_graph)
     lo, n = opt.lo, opt.n
     w, g, m, v = oracle_bufs(oracle, n, lo, SEED, scale0, heavy)
     dw, dg, dm, dv = dev(w), dev(g), dev(m), dev(v)
@@ -86,29 +85,26 @@ def tiny():
     return layout.decoder_layout("tiny", 3, 32, 72, 97)
 
 
-@pytest.mark.parametrize("two_pass", [False, True])
-def test_tiny_decoder_multi_step(oracle, two_pass):
-    st, _ = run_steps(oracle, tiny(), steps=6, inject={3: 0x7E00}, two_pass=two_pass)
+def test_tiny_decoder_multi_step(oracle):
+    st, _ = run_steps(oracle, tiny(), steps=6, inject={3: 0x7E00})
     assert st["opt_step"] == 5 and st["skipped_steps"] == 1
 
 
-@pytest.mark.parametrize("two_pass", [False, True])
-def test_compat_gamma_final_unscaled(oracle, two_pass):
-    st, _ = run_steps(oracle, tiny(), steps=3, compat=True, two_pass=two_pass)
+def test_compat_gamma_final_unscaled(oracle):
+    st, _ = run_steps(oracle, tiny(), steps=3, compat=True)
     assert st["opt_step"] == 3
 
 
-@pytest.mark.parametrize("two_pass", [False, True])
 @pytest.mark.parametrize("shard", [(1024, 8231), (0, 7), (128, 128 + 8 * 37), (0, 0)])
-def test_shard_offsets_and_ragged_sizes(oracle, shard, two_pass):
+def test_shard_offsets_and_ragged_sizes(oracle, shard):
     L = tiny()
-    run_steps(oracle, L, steps=2, shard=shard, two_pass=two_pass)
+    run_steps(oracle, L, steps=2, shard=shard)
 
 
-@pytest.mark.parametrize("n", [2048 * 296 * 3 + 8 * 5 + 3, 2048 * 7 + 8, 17])
-def test_tile_boundaries(oracle, n):
-    """Flat sizes around the persistent kernel's 2048-element tiles and its
-    per-CTA tile ranges, with a ragged tail."""
+@pytest.mark.parametrize("n", [2048 * 296 * 3 + 8 * 5 + 3, 256 * 8 * 1184 * 2 + 8, 17])
+def test_grid_stride_boundaries(oracle, n):
+    """Flat sizes around whole grid-stride sweeps (296 / 1184 blocks of 256
+    threads, 8 elements each), with a ragged tail."""
     run_steps(oracle, layout.flat_layout(n), steps=2, inject={2: 0x7C00})
 
 
@@ -135,11 +131,9 @@ def test_early_stop(oracle):
     assert st["consecutive_nans"] == 4 and st["opt_step"] == 0
 
 
-@pytest.mark.parametrize("two_pass", [False, True])
-def test_eko_full_step_bit_exact(oracle, two_pass):
+def test_eko_full_step_bit_exact(oracle):
     """EKO-237M full optimizer step, t = 1000, scale 65536."""
-    st, ost = run_steps(oracle, layout.eko_layout(), steps=1, initial_step=999, fresh_grads=False,
-                        two_pass=two_pass)
+    st, ost = run_steps(oracle, layout.eko_layout(), steps=1, initial_step=999, fresh_grads=False)
     assert st["opt_step"] == 1000 and st["last_clip_coef"] < 1.0
     assert st["last_norm"] == ost.last_norm
 
@@ -196,13 +190,20 @@ def test_bad_arguments():
     opt.close()
 
 
-def test_profile_events():
+@pytest.mark.parametrize("use_graph", [False, True])
+def test_profile_events(use_graph):
+    """Per-kernel CUDA events, also inside graph replays (event-record nodes
+    retargeted per replay)."""
     L = layout.flat_layout(10_000_000)
-    opt = ab.Optimizer(L, constant_lr=True)
+    opt = ab.Optimizer(L, constant_lr=True, use_graph=use_graph)
     bufs = synth.make_state(L.n, 0, 3, "cuda")
     opt.profile_begin(3)
     for _ in range(3):
         opt.step_all(*bufs)
     prof = opt.profile_read(3)
     assert prof.shape == (3, 3) and (prof[:, 0] > 0).all() and (prof[:, 2] > 0).all()
+    assert len(set(prof[:, 2].tolist())) > 1          # three distinct measurements
+    for _ in range(2):                                 # replays without profiling still run
+        opt.step_all(*bufs)
+    assert opt.status()["steps_called"] == 5
     opt.close()
