@@ -71,7 +71,6 @@ struct StepParams {
 };
 
 constexpr int kThreads = 256;
-constexpr int kUnroll2 = 2;   // 8-element groups in flight per thread, pass 2
 
 // --------------------------------------------------------------- pass 1
 // Exact FP16 -> FP64 widening (one conversion instruction).
@@ -362,9 +361,11 @@ __device__ __forceinline__ void update8(uint4& wq, const uint4 gq, float4& m0, f
 // Grid-stride over 8-element vectors in reverse (vector i = nvec-1-j for the
 // j-th in forward order): consecutive threads still touch consecutive
 // vectors, and the first vectors updated are the last ones pass 1 read.
-__global__ void __launch_bounds__(kThreads) pass2_kernel(StepParams p, uint16_t* __restrict__ w16,
-                                                        float* __restrict__ m,
-                                                        float* __restrict__ v) {
+template <int kUnroll2, int MINB>
+__global__ void __launch_bounds__(kThreads, MINB) pass2_kernel(StepParams p,
+                                                              uint16_t* __restrict__ w16,
+                                                              float* __restrict__ m,
+                                                              float* __restrict__ v) {
     __shared__ Plan s_plan;
     __shared__ int s_last;
     if (threadIdx.x == 0) make_plan(p, s_plan);
@@ -425,17 +426,29 @@ __global__ void __launch_bounds__(kThreads) pass2_kernel(StepParams p, uint16_t*
     if (threadIdx.x == 0) advance_state(p, pl);
 }
 
-// pass-1 variants (vectors in flight per thread, minimum resident blocks)
+// launch-shape variants: vectors in flight per thread x minimum resident blocks
 using Pass1Fn = void (*)(StepParams);
+using Pass2Fn = void (*)(StepParams, uint16_t*, float*, float*);
 struct Pass1Variant {
     int unroll, min_blocks;
     Pass1Fn fn;
+};
+struct Pass2Variant {
+    int unroll, min_blocks;
+    Pass2Fn fn;
 };
 static const Pass1Variant kPass1Variants[] = {
     {4, 4, pass1_kernel<4, 4>},
     {4, 6, pass1_kernel<4, 6>},
     {2, 8, pass1_kernel<2, 8>},
     {8, 4, pass1_kernel<8, 4>},
+    {16, 2, pass1_kernel<16, 2>},
+};
+static const Pass2Variant kPass2Variants[] = {
+    {2, 1, pass2_kernel<2, 1>},
+    {1, 3, pass2_kernel<1, 3>},
+    {1, 4, pass2_kernel<1, 4>},
+    {3, 1, pass2_kernel<3, 1>},
 };
 
 }  // namespace ark
@@ -461,7 +474,8 @@ struct ark_opt_state {
     Partial* d_part_all = nullptr;
     ark_opt_status* h_status = nullptr;  // pinned
     int blocks1 = 0, blocks2 = 0;
-    Pass1Fn pass1 = nullptr;                  // chosen pass-1 variant
+    Pass1Fn pass1 = nullptr;                  // chosen launch-shape variants
+    Pass2Fn pass2 = nullptr;
     // P2P exchange slots (world > 1)
     bool p2p = false;
     uint64_t* xchg = nullptr;                 // own receive slots (cudaMalloc, IPC-exported)
@@ -615,12 +629,15 @@ StepParams make_params(const ark_opt_state* s, const uint16_t* g16) {
     return p;
 }
 
-// Events are recorded "external" so that, under stream capture, they become
-// event-record nodes of the graph (a plain record would only order streams).
-#define ARK_RECORD(e, st) ARK_CUDA_TRY(cudaEventRecordWithFlags((e), (st), cudaEventRecordExternal))
+// Under stream capture, events are recorded "external" so that they become
+// event-record nodes of the graph (a plain record would only order streams);
+// the external flag is only valid while capturing.
+#define ARK_RECORD(e, st)                                                                   \
+    ARK_CUDA_TRY(capturing ? cudaEventRecordWithFlags((e), (st), cudaEventRecordExternal) \
+                           : cudaEventRecord((e), (st)))
 
 int enqueue_step(ark_opt_state* s, cudaStream_t stream, uint16_t* w16, const uint16_t* g16,
-                 float* m, float* v, cudaEvent_t* ev) {
+                 float* m, float* v, cudaEvent_t* ev, bool capturing = false) {
     StepParams p = make_params(s, g16);
     if (ev) ARK_RECORD(ev[0], stream);
     s->pass1<<<s->blocks1, kThreads, 0, stream>>>(p);
@@ -635,7 +652,7 @@ int enqueue_step(ark_opt_state* s, cudaStream_t stream, uint16_t* w16, const uin
         }
     }
     if (ev) ARK_RECORD(ev[2], stream);
-    pass2_kernel<<<s->blocks2, kThreads, 0, stream>>>(p, w16, m, v);
+    s->pass2<<<s->blocks2, kThreads, 0, stream>>>(p, w16, m, v);
     ARK_CUDA_TRY(cudaGetLastError());
     if (ev) ARK_RECORD(ev[3], stream);
     return ARK_OK;
@@ -661,7 +678,8 @@ int capture_graph(ark_opt_state* s, int slot, uint16_t* w16, const uint16_t* g16
         for (auto& e : s->ph_ev) ARK_CUDA_TRY(cudaEventCreate(&e));
     cudaGraph_t g = nullptr;
     ARK_CUDA_TRY(cudaStreamBeginCapture(s->capture_stream, cudaStreamCaptureModeThreadLocal));
-    const int rc = enqueue_step(s, s->capture_stream, w16, g16, m, v, slot ? s->ph_ev : nullptr);
+    const int rc =
+        enqueue_step(s, s->capture_stream, w16, g16, m, v, slot ? s->ph_ev : nullptr, true);
     const cudaError_t e = cudaStreamEndCapture(s->capture_stream, &g);
     if (rc != ARK_OK) {
         if (g) cudaGraphDestroy(g);
@@ -732,8 +750,14 @@ int ark_cuda_opt_init(const ark_opt_cfg* cfg, ark_opt_state** out) {
     s->pass1 = kPass1Variants[var].fn;
     s->blocks1 = streaming_grid(reinterpret_cast<const void*>(s->pass1), kThreads, 0,
                                 (cfg->n >> 3) / kPass1Variants[var].unroll + 1);
-    s->blocks2 = streaming_grid(reinterpret_cast<const void*>(pass2_kernel), kThreads, 0,
-                                (cfg->n >> 3) / kUnroll2 + 1);
+    // pass 2: 2 groups in flight x 2 blocks/SM for large shards, 1 group x 3
+    // blocks/SM below 100M params (shorter tail; EKO/4 and EKO/8 sweep)
+    int var2 = cfg->n < 100000000ull ? 1 : 0;
+    if (const char* e = getenv("ARK_PASS2_VARIANT")) var2 = atoi(e);
+    if (var2 < 0 || var2 >= (int)(sizeof(kPass2Variants) / sizeof(kPass2Variants[0]))) var2 = 0;
+    s->pass2 = kPass2Variants[var2].fn;
+    s->blocks2 = streaming_grid(reinterpret_cast<const void*>(s->pass2), kThreads, 0,
+                                (cfg->n >> 3) / kPass2Variants[var2].unroll + 1);
     const int W = cfg->world_size;
     s->timeout_ns = (uint64_t)(cfg->wait_timeout_ms ? cfg->wait_timeout_ms : 5000u) * 1000000ull;
     const int nblk = s->blocks1;
