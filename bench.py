@@ -280,7 +280,16 @@ def run_ours(args):
     if world > 1:
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
-    L = layout.flat_layout(args.params) if args.params else layout.eko_layout()
+    if args.params:
+        L = layout.flat_layout(args.params)
+        workload = f"flat buffer of {L.n} params (BASELINE configs[4])"
+    else:
+        L = layout.LAYOUTS[args.workload]()
+        workload = {"eko": "EKO-237M full optimizer step (BASELINE configs[0])",
+                    "1.3b": "1.3B decoder, ZeRO-1 sharded (BASELINE configs[2])",
+                    "7b": "7B decoder, 1% of grads x100 so clipping is active, ZeRO-1 sharded "
+                          "(BASELINE configs[3])"}[args.workload]
+    heavy = args.workload == "7b" and not args.params
     comm = adist.nccl_comm(rank, world, local) if world > 1 else None
     adam = ab.AdamConfig(**EKO_HPARAMS)
     scale = ab.LossScaleConfig(init=LOSS_SCALE, every=2000, max=2.0 ** 24)
@@ -289,7 +298,7 @@ def run_ours(args):
                        stream=stream, constant_lr=True, initial_step=START_STEP - 1,
                        use_graph=args.graph, nccl_exchange=args.nccl_exchange)
     lo, n = opt.lo, opt.n
-    w16, g16, m, v = synth.make_state(n, lo, SEED, dev, loss_scale=LOSS_SCALE)
+    w16, g16, m, v = synth.make_state(n, lo, SEED, dev, loss_scale=LOSS_SCALE, heavy=heavy)
     torch.cuda.synchronize()
 
     def barrier():
@@ -367,7 +376,8 @@ def run_ours(args):
     geom = opt.geometry()
 
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline and not args.params:
+    if (rank == 0 and world == 1 and not args.no_cpu_baseline and not args.params
+            and args.workload == "eko"):
         cpu = cpu_baseline_single_thread(L)
 
     if rank == 0:
@@ -379,9 +389,7 @@ def run_ours(args):
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded splitmix64 + Irwin-Hall normals with the BASELINE "
                     "distributions, generated on the device)",
-            "config": {"workload": ("EKO-237M full optimizer step (BASELINE configs[0])"
-                                    if not args.params else
-                                    f"flat buffer of {L.n} params (BASELINE configs[4])"),
+            "config": {"workload": workload,
                        "params": L.n, "params_per_gpu": n, "tensors": L.n_tensors,
                        "parallelism": f"zero1-dp{world}", "t": START_STEP,
                        "loss_scale": LOSS_SCALE, "clip": "active",
@@ -417,6 +425,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--params", type=int, default=0,
                     help="flat-buffer workload of this many params instead of EKO-237M")
+    ap.add_argument("--workload", choices=("eko", "1.3b", "7b"), default="eko",
+                    help="model layout (BASELINE configs 0, 2, 3); the headline is eko")
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-graph", dest="graph", action="store_false",
                     help="launch the kernels directly instead of replaying a CUDA graph")

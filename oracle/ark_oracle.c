@@ -266,18 +266,35 @@ ORK_API void ork_partial_f16(const ork_step_cfg* cfg, const ork_amp_state* st,
                              const uint16_t* g16, uint64_t n, uint64_t offset,
                              double* sumsq, uint64_t* nonfinite) {
     float inv = 1.0f / st->loss_scale;                  /* training.rs:244 */
-    ork_acc a = {0.0, 0.0};
+    /* Compensated sums over fixed chunks (in parallel), combined in chunk
+     * order with the same compensation: exact to ~2^-100, independent of the
+     * thread count. */
+    const uint64_t chunk = 1u << 20;
+    const int64_t nchunks = (int64_t)((n + chunk - 1) / chunk);
+    ork_acc* parts = (ork_acc*)calloc(nchunks > 0 ? (size_t)nchunks : 1, sizeof(ork_acc));
     uint64_t bad = 0;
-    for (uint64_t i = 0; i < n; ++i) {
-        uint16_t h = g16[i];
-        if ((h & 0x7C00u) == 0x7C00u) { bad++; continue; }
-        uint64_t gi = offset + i;
-        float u = ork_h2f(h);
-        if (!(gi >= cfg->keep_lo && gi < cfg->keep_hi)) u = u * inv;
-        double d = (double)u;
-        acc_add(&a, d * d);
+    #pragma omp parallel for schedule(dynamic, 4) reduction(+:bad)
+    for (int64_t c = 0; c < nchunks; ++c) {
+        ork_acc a = {0.0, 0.0};
+        uint64_t lo = (uint64_t)c * chunk, hi = lo + chunk < n ? lo + chunk : n;
+        for (uint64_t i = lo; i < hi; ++i) {
+            uint16_t h = g16[i];
+            if ((h & 0x7C00u) == 0x7C00u) { bad++; continue; }
+            uint64_t gi = offset + i;
+            float u = ork_h2f(h);
+            if (!(gi >= cfg->keep_lo && gi < cfg->keep_hi)) u = u * inv;
+            double d = (double)u;
+            acc_add(&a, d * d);
+        }
+        parts[c] = a;
     }
-    *sumsq = acc_value(&a);
+    ork_acc tot = {0.0, 0.0};
+    for (int64_t c = 0; c < nchunks; ++c) {
+        acc_add(&tot, parts[c].s);
+        acc_add(&tot, parts[c].c);
+    }
+    free(parts);
+    *sumsq = acc_value(&tot);
     *nonfinite = bad;
 }
 
@@ -314,8 +331,9 @@ ORK_API int ork_apply_f16(const ork_step_cfg* cfg, ork_amp_state* st,
     ork_adam_k kd, k0;
     ork_adam_scalars(lr, cfg->beta1, cfg->beta2, cfg->eps, cfg->weight_decay, t, &kd);
     ork_adam_scalars(lr, cfg->beta1, cfg->beta2, cfg->eps, 0.0f, t, &k0);  /* optimizer.rs:199,225-226 */
-    for (uint64_t i = 0; i < n; ++i) {
-        uint64_t gi = offset + i;
+    #pragma omp parallel for schedule(static)
+    for (int64_t ii = 0; ii < (int64_t)n; ++ii) {
+        uint64_t i = (uint64_t)ii, gi = offset + i;
         float g = ork_h2f(g16[i]);
         if (!(gi >= cfg->keep_lo && gi < cfg->keep_hi)) g = g * inv;     /* training.rs:308 */
         if (clip) g = g * s;                                              /* optimizer.rs:151-166 */
