@@ -21,6 +21,7 @@ SCALE = 65536.0
 
 
 def _fits(n):
+    torch.cuda.empty_cache()
     free, _ = torch.cuda.mem_get_info()
     return free > n * 14 * 1.08 + (2 << 30)
 
