@@ -14,6 +14,8 @@ import torch.multiprocessing as mp
 pytestmark = pytest.mark.gpu
 
 WORLD = 2
+# world sizes of the parity test: 2, and 4 / 8 where that many GPUs are visible
+WORLDS = [w for w in (2, 4, 8) if w <= max(torch.cuda.device_count(), 2)]
 
 
 def _free_port():
@@ -77,17 +79,20 @@ def _rank_main(rank, world, port, q, nccl_exchange):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason="needs 2 GPUs")
+@pytest.mark.parametrize("world", WORLDS)
 @pytest.mark.parametrize("nccl_exchange", [False, True])
-def test_two_gpu_zero1_step_matches_oracle(oracle, nccl_exchange):
+def test_multi_gpu_zero1_step_matches_oracle(oracle, nccl_exchange, world):
     from ark_b200 import layout, synth
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     port = _free_port()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_rank_main, args=(r, WORLD, port, q, nccl_exchange))
-             for r in range(WORLD)]
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, q, nccl_exchange))
+             for r in range(world)]
     for p in procs:
         p.start()
-    res = sorted([q.get(timeout=300) for _ in range(WORLD)], key=lambda r: r[0])
+    res = sorted([q.get(timeout=300) for _ in range(world)], key=lambda r: r[0])
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
@@ -122,7 +127,7 @@ def test_two_gpu_zero1_step_matches_oracle(oracle, nccl_exchange):
             assert abs(a[4] - b[4]) <= 1e-5 * max(b[4], 1e-30)
         for r2, lo2, hi2, *_ in res:                      # all-gathered weights
             assert np.array_equal(full[r2 * stride: r2 * stride + (hi2 - lo2)], w[lo2:hi2])
-    assert res[0][6][-1] == res[1][6][-1]                 # replicated state identical
+    assert all(r[6][-1] == res[0][6][-1] for r in res)    # replicated state identical
 
 
 def _timeout_rank_main(rank, world, port, q, go):
