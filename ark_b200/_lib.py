@@ -75,6 +75,8 @@ SIGNATURES = {
     "ark_cuda_abi_version": (c_u32, []),
     "ark_cuda_opt_init": (c_i, [ctypes.POINTER(OptCfg), ctypes.POINTER(c_p)]),
     "ark_cuda_opt_step": (c_i, [c_p, c_p, c_p, c_p, c_p]),
+    "ark_cuda_opt_grad_buffer": (c_i, [c_p, c_u64, ctypes.POINTER(c_p)]),
+    "ark_cuda_opt_step_reduce": (c_i, [c_p, c_p, c_p, c_p, c_p]),
     "ark_cuda_opt_read_status": (c_i, [c_p, ctypes.POINTER(OptStatus)]),
     "ark_cuda_opt_set_status": (c_i, [c_p, ctypes.POINTER(OptStatus)]),
     "ark_cuda_opt_upload_grads": (c_i, [c_p, c_p, c_p, c_u64]),

@@ -68,6 +68,9 @@ struct StepParams {
     uint64_t* xchg;                  // own receive slots [2][world] x {sum, bad, epoch, pad}
     uint64_t* const* peers;          // every rank's receive slots (peers[rank] == xchg)
     uint64_t peer_timeout_ns;
+    // reduce-scatter step: every rank's full FP16 gradient buffer (mapped here)
+    const uint16_t* const* gsrc;
+    uint16_t* g16_out;               // this rank's reduced shard
 };
 
 constexpr int kThreads = 256;
@@ -129,6 +132,13 @@ __device__ __forceinline__ void accum8_pow2(uint4 q, uint64_t gi0, uint64_t keep
     }
 }
 
+// Receive slot of rank q in rank r's buffer, for one epoch parity: 4 x u64
+// {sum of squares, non-finite, partial epoch, gradients-ready epoch}.
+__device__ __forceinline__ uint64_t* slot_of(uint64_t* base, unsigned long long epoch, int world,
+                                             int q) {
+    return base + (((epoch & 1ull) * (unsigned long long)world + (unsigned long long)q) * 4);
+}
+
 // Last pass-1 block, world > 1 over mapped peer slots: lane r (< world) of
 // warp 0 stores this rank's partial into rank r's slot [epoch & 1][rank]
 // (payload, then the epoch with release semantics) and waits, bounded by
@@ -139,10 +149,10 @@ __device__ void exchange_p2p(const StepParams& p, double my_sum, unsigned long l
     const int r = threadIdx.x;
     if (r >= p.world) return;
     const unsigned long long epoch = p.st->steps_called + 1ull;
-    uint64_t* dst = p.peers[r] + (((epoch & 1ull) * p.world + p.rank) * 4);
+    uint64_t* dst = slot_of(p.peers[r], epoch, p.world, p.rank);
     st_relaxed_sys_v2(dst, (uint64_t)__double_as_longlong(my_sum), my_bad);
     st_release_sys(dst + 2, epoch);
-    const uint64_t* src = p.xchg + (((epoch & 1ull) * p.world + r) * 4);
+    const uint64_t* src = slot_of(p.xchg, epoch, p.world, r);
     const uint64_t t0 = global_ns();
     bool ok = true;
     while (ld_acquire_sys(src + 2) != epoch) {
@@ -165,17 +175,103 @@ __device__ void exchange_p2p(const StepParams& p, double my_sum, unsigned long l
     p.part_all[r] = got;
 }
 
-template <int U, int MINB>
-__global__ void __launch_bounds__(kThreads, MINB) pass1_kernel(StepParams p) {
+// Per-thread pass-1 accumulators.
+struct P1Acc {
+    double acc0 = 0.0, acc1 = 0.0, acc_k = 0.0;
+    uint32_t amax = 0;
+};
+
+struct P1Scale {
+    float inv;
+    bool pow2;
+};
+
+__device__ __forceinline__ P1Scale p1_scale(const StepParams& p) {
+    P1Scale sc;
+    sc.inv = __fdiv_rn(1.0f, p.st->loss_scale);   // training.rs:244
+    const uint32_t ib = __float_as_uint(sc.inv);
+    sc.pow2 = (ib & 0x7FFFFFu) == 0 && (ib & 0x7F800000u) != 0 &&
+              (ib & 0x7F800000u) != 0x7F800000u;
+    return sc;
+}
+
+__device__ __forceinline__ void p1_consume(P1Acc& a, const uint4 q, uint64_t vec,
+                                           const P1Scale& sc, const StepParams& p) {
+    a.amax = absmax2(a.amax, q.x);
+    a.amax = absmax2(a.amax, q.y);
+    a.amax = absmax2(a.amax, q.z);
+    a.amax = absmax2(a.amax, q.w);
+    const uint64_t gi0 = p.offset + (vec << 3);
+    if (sc.pow2) accum8_pow2(q, gi0, p.keep_lo, p.keep_hi, a.acc0, a.acc1, a.acc_k);
+    else accum8_general(q, gi0, sc.inv, p.keep_lo, p.keep_hi, a.acc0, a.acc1);
+}
+
+__device__ __forceinline__ void p1_consume1(P1Acc& a, uint16_t h, uint64_t i, const P1Scale& sc,
+                                            const StepParams& p) {
+    a.amax = absmax2(a.amax, h);
+    const uint64_t gi = p.offset + i;
+    const bool keep = gi >= p.keep_lo && gi < p.keep_hi;
+    if (sc.pow2) {
+        const double d = h2d(h);
+        if (keep) a.acc_k = __fma_rn(d, d, a.acc_k);
+        else a.acc0 = __fma_rn(d, d, a.acc0);
+    } else {
+        const float f = h2f(h);
+        const double d = (double)(keep ? f : __fmul_rn(f, sc.inv));
+        a.acc0 = __fma_rn(d, d, a.acc0);
+    }
+}
+
+// Block reduction, last-block fixed-order reduction and the rank exchange.
+// `failed` (any thread) marks this rank's partial as unusable.
+__device__ void p1_finish(const P1Acc& a, const P1Scale& sc, bool failed, const StepParams& p) {
     __shared__ double s_sum[kThreads / 32];
     __shared__ unsigned long long s_bad[kThreads / 32];
     __shared__ int s_last;
-    const float inv = __fdiv_rn(1.0f, p.st->loss_scale);   // training.rs:244
-    const uint32_t ib = __float_as_uint(inv);
-    const bool pow2 = (ib & 0x7FFFFFu) == 0 && (ib & 0x7F800000u) != 0 &&
-                      (ib & 0x7F800000u) != 0x7F800000u;
-    double acc0 = 0.0, acc1 = 0.0, acc_k = 0.0;
-    uint32_t amax = 0;
+    // fold the power-of-two scaling in per thread (exact): sum of u^2
+    const double inv_d = (double)sc.inv;
+    const double acc_s = a.acc0 + a.acc1;
+    const double acc = sc.pow2 ? __fma_rn(acc_s, inv_d * inv_d, a.acc_k) : acc_s;
+    const unsigned long long bad =
+        ((a.amax & 0xFFFFu) >= 0x7C00u) || ((a.amax >> 16) >= 0x7C00u);
+    const double bsum = block_sum<kThreads>(acc, s_sum);
+    const unsigned long long bbad = block_sum_u64<kThreads>(bad, s_bad);
+    const unsigned long long bfail = block_sum_u64<kThreads>(failed ? 1ull : 0ull, s_bad);
+    if (threadIdx.x == 0) {
+        p.blk_sum[blockIdx.x] = bsum;
+        p.blk_bad[blockIdx.x] = bfail ? kPartialTimeout : bbad;
+    }
+    if (!last_block_arrived(p.ticket1, &s_last)) return;
+    // Last block: fixed-order reduction of the per-block partials.
+    double s = 0.0;
+    unsigned long long b = 0, f = 0;
+    for (unsigned int i = threadIdx.x; i < gridDim.x; i += kThreads) {
+        s += __ldcg(p.blk_sum + i);
+        const unsigned long long x = __ldcg(p.blk_bad + i);
+        if (x == kPartialTimeout) f = 1;
+        else b += x;
+    }
+    s = block_sum<kThreads>(s, s_sum);
+    b = block_sum_u64<kThreads>(b, s_bad);
+    f = block_sum_u64<kThreads>(f, s_bad);
+    if (f) b = kPartialTimeout;
+    if (p.p2p) {
+        if (threadIdx.x == 0) {
+            s_sum[0] = s;
+            s_bad[0] = b;
+        }
+        __syncthreads();
+        if (threadIdx.x < kMaxP2PRanks) exchange_p2p(p, s_sum[0], s_bad[0]);
+    } else if (threadIdx.x == 0) {
+        p.part_local->sumsq = s;
+        p.part_local->nonfinite = b;   // threads that saw an inf/NaN (> 0 iff any)
+    }
+}
+
+template <int U, int MINB>
+__global__ void __launch_bounds__(kThreads, MINB) pass1_kernel(StepParams p) {
+    const P1Scale sc = p1_scale(p);
+    P1Acc a;
     const uint4* g = reinterpret_cast<const uint4*>(p.g16);
     const uint64_t nvec = p.n >> 3;
     const uint64_t stride = (uint64_t)gridDim.x * kThreads;
@@ -189,66 +285,107 @@ __global__ void __launch_bounds__(kThreads, MINB) pass1_kernel(StepParams p) {
         }
 #pragma unroll
         for (int u = 0; u < U; ++u) {
-            amax = absmax2(amax, q[u].x);
-            amax = absmax2(amax, q[u].y);
-            amax = absmax2(amax, q[u].z);
-            amax = absmax2(amax, q[u].w);
             const uint64_t i = base + u * stride;
-            if (i < nvec) {
-                if (pow2) accum8_pow2(q[u], p.offset + (i << 3), p.keep_lo, p.keep_hi, acc0, acc1, acc_k);
-                else accum8_general(q[u], p.offset + (i << 3), inv, p.keep_lo, p.keep_hi, acc0, acc1);
+            if (i < nvec) p1_consume(a, q[u], i, sc, p);
+        }
+    }
+    if (blockIdx.x == 0 && threadIdx.x < (p.n & 7u)) {   // ragged tail (n % 8)
+        const uint64_t i = (nvec << 3) + threadIdx.x;
+        p1_consume1(a, p.g16[i], i, sc, p);
+    }
+    p1_finish(a, sc, false, p);
+}
+
+// The gradient hand-off fused with pass 1: this rank's shard of the sum over
+// ranks of every rank's full FP16 gradient buffer, read straight from the
+// peers' memory over NVLink.  The reference zeroes its FP32 gradients and
+// accumulates the backward's output with += (src/memory.rs:338-342,
+// objc/bridge.m:907-949); here the contributions of the ranks are
+// accumulated in FP32 in rank order starting from 0, rounded once to FP16
+// (RNE) into the local shard, and finite-checked / squared from the same
+// registers.  Before reading, each rank announces that its buffer is
+// complete (gradients-ready epoch in every peer's slot) and waits, bounded,
+// for every peer's announcement; the partial exchange at the end of pass 1
+// then proves that every peer has finished reading this rank's buffer.
+template <int U, int MINB>
+__global__ void __launch_bounds__(kThreads, MINB) pass1_reduce_kernel(StepParams p) {
+    __shared__ int s_fail;
+    const unsigned long long epoch = p.st->steps_called + 1ull;
+    if (threadIdx.x == 0) s_fail = 0;
+    if (p.world > 1) {
+        if (blockIdx.x == 0 && threadIdx.x < p.world) {
+            __threadfence_system();
+            st_release_sys(slot_of(p.peers[threadIdx.x], epoch, p.world, p.rank) + 3, epoch);
+        }
+        if (threadIdx.x == 0) {
+            const uint64_t t0 = global_ns();
+            for (int q = 0; q < p.world && !s_fail; ++q) {
+                const uint64_t* ready = slot_of(p.xchg, epoch, p.world, q) + 3;
+                while (ld_acquire_sys(ready) != epoch) {
+                    if (global_ns() - t0 > p.peer_timeout_ns) {
+                        s_fail = 1;
+                        break;
+                    }
+                    __nanosleep(64);
+                }
             }
         }
     }
-    // ragged tail (n % 8 elements)
-    if (blockIdx.x == 0 && threadIdx.x < (p.n & 7u)) {
-        const uint64_t i = (nvec << 3) + threadIdx.x;
-        const uint16_t h = p.g16[i];
-        amax = absmax2(amax, h);
-        const uint64_t gi = p.offset + i;
-        const bool keep = gi >= p.keep_lo && gi < p.keep_hi;
-        if (pow2) {
-            const double d = h2d(h);
-            if (keep) acc_k = __fma_rn(d, d, acc_k);
-            else acc0 = __fma_rn(d, d, acc0);
-        } else {
-            const float f = h2f(h);
-            const double d = (double)(keep ? f : __fmul_rn(f, inv));
-            acc0 = __fma_rn(d, d, acc0);
+    __syncthreads();
+    const bool failed = s_fail != 0;
+    const P1Scale sc = p1_scale(p);
+    P1Acc a;
+    const uint64_t nvec = p.n >> 3;
+    const uint64_t stride = (uint64_t)gridDim.x * kThreads;
+    uint4* out = reinterpret_cast<uint4*>(p.g16_out);
+    if (!failed) {
+        for (uint64_t base = (uint64_t)blockIdx.x * kThreads + threadIdx.x; base < nvec;
+             base += stride * U) {
+            float acc[U][8];
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+#pragma unroll
+                for (int j = 0; j < 8; ++j) acc[u][j] = 0.0f;
+            for (int r = 0; r < p.world; ++r) {                 // rank order
+                const uint4* src = reinterpret_cast<const uint4*>(p.gsrc[r] + p.offset);
+                uint4 q[U];
+#pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    const uint64_t i = base + u * stride;
+                    q[u] = i < nvec ? __ldcg(src + i) : make_uint4(0, 0, 0, 0);
+                }
+#pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    const uint32_t w[4] = {q[u].x, q[u].y, q[u].z, q[u].w};
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        acc[u][j] = __fadd_rn(acc[u][j],
+                                              h2f((j & 1) ? hi16(w[j >> 1]) : lo16(w[j >> 1])));
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const uint64_t i = base + u * stride;
+                if (i < nvec) {
+                    uint32_t w[4];
+#pragma unroll
+                    for (int k = 0; k < 4; ++k) w[k] = pack16(f2h(acc[u][2 * k]), f2h(acc[u][2 * k + 1]));
+                    const uint4 rq = make_uint4(w[0], w[1], w[2], w[3]);
+                    out[i] = rq;
+                    p1_consume(a, rq, i, sc, p);
+                }
+            }
+        }
+        if (blockIdx.x == 0 && threadIdx.x < (p.n & 7u)) {   // ragged tail (n % 8)
+            const uint64_t i = (nvec << 3) + threadIdx.x;
+            float f = 0.0f;
+            for (int r = 0; r < p.world; ++r) f = __fadd_rn(f, h2f(p.gsrc[r][p.offset + i]));
+            const uint16_t h = f2h(f);
+            p.g16_out[i] = h;
+            p1_consume1(a, h, i, sc, p);
         }
     }
-    // fold the power-of-two scaling in per thread (exact): sum of u^2
-    const double inv_d = (double)inv;
-    const double acc_s = acc0 + acc1;
-    const double acc = pow2 ? __fma_rn(acc_s, inv_d * inv_d, acc_k) : acc_s;
-    const unsigned long long bad = ((amax & 0xFFFFu) >= 0x7C00u) || ((amax >> 16) >= 0x7C00u);
-    const double bsum = block_sum<kThreads>(acc, s_sum);
-    const unsigned long long bbad = block_sum_u64<kThreads>(bad, s_bad);
-    if (threadIdx.x == 0) {
-        p.blk_sum[blockIdx.x] = bsum;
-        p.blk_bad[blockIdx.x] = bbad;
-    }
-    if (!last_block_arrived(p.ticket1, &s_last)) return;
-    // Last block: fixed-order reduction of the per-block partials.
-    double a = 0.0;
-    unsigned long long b = 0;
-    for (unsigned int i = threadIdx.x; i < gridDim.x; i += kThreads) {
-        a += __ldcg(p.blk_sum + i);
-        b += __ldcg(p.blk_bad + i);
-    }
-    a = block_sum<kThreads>(a, s_sum);
-    b = block_sum_u64<kThreads>(b, s_bad);
-    if (p.p2p) {
-        if (threadIdx.x == 0) {
-            s_sum[0] = a;
-            s_bad[0] = b;
-        }
-        __syncthreads();
-        if (threadIdx.x < kMaxP2PRanks) exchange_p2p(p, s_sum[0], s_bad[0]);
-    } else if (threadIdx.x == 0) {
-        p.part_local->sumsq = a;
-        p.part_local->nonfinite = b;   // threads that saw an inf/NaN (> 0 iff any)
-    }
+    p1_finish(a, sc, failed, p);
 }
 
 // --------------------------------------------------------------- pass 2
@@ -444,6 +581,7 @@ static const Pass1Variant kPass1Variants[] = {
     {8, 4, pass1_kernel<8, 4>},
     {16, 2, pass1_kernel<16, 2>},
 };
+static const Pass1Fn kPass1Reduce = pass1_reduce_kernel<2, 4>;
 static const Pass2Variant kPass2Variants[] = {
     {2, 1, pass2_kernel<2, 1>},
     {1, 3, pass2_kernel<1, 3>},
@@ -473,7 +611,7 @@ struct ark_opt_state {
     Partial* d_part_local = nullptr;
     Partial* d_part_all = nullptr;
     ark_opt_status* h_status = nullptr;  // pinned
-    int blocks1 = 0, blocks2 = 0;
+    int blocks1 = 0, blocks2 = 0, blocks1r = 0;
     Pass1Fn pass1 = nullptr;                  // chosen launch-shape variants
     Pass2Fn pass2 = nullptr;
     // P2P exchange slots (world > 1)
@@ -481,14 +619,20 @@ struct ark_opt_state {
     uint64_t* xchg = nullptr;                 // own receive slots (cudaMalloc, IPC-exported)
     std::vector<uint64_t*> peer_slots;        // every rank's slots, mapped here
     uint64_t** d_peers = nullptr;             // device copy of peer_slots
+    // full-gradient buffers of the reduce-scatter step (world >= 1)
+    void* gbuf = nullptr;                     // this rank's buffer (cudaMalloc, IPC-exported)
+    uint64_t gbuf_n = 0;
+    std::vector<void*> gpeer;                 // every rank's buffer, mapped here
+    const uint16_t** d_gsrc = nullptr;        // device copy of gpeer
     uint64_t timeout_ns = 0;
     // graph replay
     // graph replay: slot 0 plain, slot 1 with four event-record nodes that are
     // pointed at the profiling events of each replay
-    cudaGraph_t gsrc[2] = {nullptr, nullptr};
-    cudaGraphExec_t gexec[2] = {nullptr, nullptr};
-    const void* gkey[2][4] = {{nullptr, nullptr, nullptr, nullptr}, {nullptr, nullptr, nullptr, nullptr}};
-    cudaGraphNode_t ev_node[4] = {nullptr, nullptr, nullptr, nullptr};
+    // (slots 2 and 3: the same for the reduce-scatter step)
+    cudaGraph_t gsrc[4] = {nullptr, nullptr, nullptr, nullptr};
+    cudaGraphExec_t gexec[4] = {nullptr, nullptr, nullptr, nullptr};
+    const void* gkey[4][4] = {};
+    cudaGraphNode_t ev_node[2][4] = {};     // per profiled slot (1, 3)
     cudaEvent_t ph_ev[4] = {nullptr, nullptr, nullptr, nullptr};   // capture placeholders
     cudaStream_t capture_stream = nullptr;
     // profiling
@@ -518,64 +662,87 @@ int check_cfg(const ark_opt_cfg* c) {
 // communicator, and every rank maps its peers' slots.  All ranks then agree
 // (NCCL min-reduction) whether every mapping succeeded; if not, every rank
 // exchanges the partials with an NCCL all-gather instead.
-int setup_p2p(ark_opt_state* s) {
+// Collective over the rank's NCCL communicator: export `local` (the base
+// of a cudaMalloc allocation) through CUDA IPC, all-gather the handles, map
+// every peer's allocation here (mapped[rank] = local), and agree with an
+// NCCL min-reduction whether every rank mapped every peer.  On disagreement
+// the mappings made here are closed again and *all_ok is false on every rank.
+int share_ipc(ark_opt_state* s, void* local, std::vector<void*>& mapped, bool* all_ok) {
     const int W = s->cfg.world_size, R = s->cfg.rank;
-    if (W < 2 || W > kMaxP2PRanks || !s->comm) return ARK_OK;
-    const size_t slot_bytes = sizeof(uint64_t) * 4 * 2 * (size_t)W;
-    int ok = 1;
-    char* d_tmp = nullptr;   // [W] handles | ok flag
-    if (cudaMalloc(&s->xchg, slot_bytes) != cudaSuccess) ok = 0;
-    if (ok && cudaMemset(s->xchg, 0, slot_bytes) != cudaSuccess) ok = 0;
+    *all_ok = false;
+    mapped.assign(W, nullptr);
+    int ok = local != nullptr;
     cudaIpcMemHandle_t mine;
     memset(&mine, 0, sizeof(mine));
-    if (ok && cudaIpcGetMemHandle(&mine, s->xchg) != cudaSuccess) ok = 0;
+    if (ok && cudaIpcGetMemHandle(&mine, local) != cudaSuccess) {
+        cudaGetLastError();
+        ok = 0;
+    }
     const size_t hb = sizeof(cudaIpcMemHandle_t);
+    char* d_tmp = nullptr;   // [W] handles | agreement flag
     if (cudaMalloc(&d_tmp, hb * W + 256) != cudaSuccess) return ARK_E_CUDA;
     int* d_ok = reinterpret_cast<int*>(d_tmp + hb * W);
+    int rc = ARK_OK;
     std::vector<cudaIpcMemHandle_t> all(W);
     cudaMemcpy(d_tmp + hb * R, &mine, hb, cudaMemcpyHostToDevice);
-    if (ncclAllGather(d_tmp + hb * R, d_tmp, hb, ncclUint8, s->comm, s->stream) != ncclSuccess) {
-        cudaFree(d_tmp);
-        return ARK_E_NCCL;
+    if (ncclAllGather(d_tmp + hb * R, d_tmp, hb, ncclUint8, s->comm, s->stream) != ncclSuccess)
+        rc = ARK_E_NCCL;
+    else if (cudaStreamSynchronize(s->stream) != cudaSuccess)
+        rc = ARK_E_CUDA;
+    if (rc == ARK_OK) {
+        cudaMemcpy(all.data(), d_tmp, hb * W, cudaMemcpyDeviceToHost);
+        for (int r = 0; r < W && ok; ++r) {
+            if (r == R) {
+                mapped[r] = local;
+                continue;
+            }
+            if (cudaIpcOpenMemHandle(&mapped[r], all[r], cudaIpcMemLazyEnablePeerAccess) !=
+                cudaSuccess) {
+                cudaGetLastError();
+                mapped[r] = nullptr;
+                ok = 0;
+            }
+        }
+        cudaMemcpy(d_ok, &ok, sizeof(int), cudaMemcpyHostToDevice);
+        if (ncclAllReduce(d_ok, d_ok, 1, ncclInt32, ncclMin, s->comm, s->stream) != ncclSuccess)
+            rc = ARK_E_NCCL;
+        else if (cudaStreamSynchronize(s->stream) != cudaSuccess)
+            rc = ARK_E_CUDA;
+        int agreed = 0;
+        if (rc == ARK_OK) cudaMemcpy(&agreed, d_ok, sizeof(int), cudaMemcpyDeviceToHost);
+        *all_ok = rc == ARK_OK && agreed != 0;
     }
-    if (cudaStreamSynchronize(s->stream) != cudaSuccess) {
-        cudaFree(d_tmp);
-        return ARK_E_CUDA;
+    cudaFree(d_tmp);
+    if (!*all_ok) {
+        for (int r = 0; r < W; ++r)
+            if (mapped[r] && mapped[r] != local) cudaIpcCloseMemHandle(mapped[r]);
+        mapped.assign(W, nullptr);
     }
-    cudaMemcpy(all.data(), d_tmp, hb * W, cudaMemcpyDeviceToHost);
+    return rc;
+}
+
+// Exchange-slot set-up for world > 1: each rank's receive slots are shared
+// through share_ipc; if any rank cannot map its peers, every rank exchanges
+// the partials with an NCCL all-gather instead.
+int setup_p2p(ark_opt_state* s) {
+    const int W = s->cfg.world_size;
+    if (W < 2 || W > kMaxP2PRanks || !s->comm) return ARK_OK;
+    const size_t slot_bytes = sizeof(uint64_t) * 4 * 2 * (size_t)W;
+    if (cudaMalloc(&s->xchg, slot_bytes) != cudaSuccess) s->xchg = nullptr;
+    else if (cudaMemset(s->xchg, 0, slot_bytes) != cudaSuccess) return ARK_E_CUDA;
+    std::vector<void*> mapped;
+    bool all_ok = false;
+    const int rc = share_ipc(s, s->xchg, mapped, &all_ok);
+    if (rc) return rc;
     s->peer_slots.assign(W, nullptr);
-    for (int r = 0; r < W && ok; ++r) {
-        if (r == R) {
-            s->peer_slots[r] = s->xchg;
-            continue;
-        }
-        void* p = nullptr;
-        if (cudaIpcOpenMemHandle(&p, all[r], cudaIpcMemLazyEnablePeerAccess) != cudaSuccess) {
-            cudaGetLastError();
-            ok = 0;
-            break;
-        }
-        s->peer_slots[r] = static_cast<uint64_t*>(p);
-    }
-    if (ok) {
+    if (all_ok) {
+        for (int r = 0; r < W; ++r) s->peer_slots[r] = static_cast<uint64_t*>(mapped[r]);
         if (cudaMalloc(&s->d_peers, sizeof(uint64_t*) * W) != cudaSuccess ||
             cudaMemcpy(s->d_peers, s->peer_slots.data(), sizeof(uint64_t*) * W,
                        cudaMemcpyHostToDevice) != cudaSuccess)
-            ok = 0;
+            return ARK_E_CUDA;
     }
-    cudaMemcpy(d_ok, &ok, sizeof(int), cudaMemcpyHostToDevice);
-    if (ncclAllReduce(d_ok, d_ok, 1, ncclInt32, ncclMin, s->comm, s->stream) != ncclSuccess) {
-        cudaFree(d_tmp);
-        return ARK_E_NCCL;
-    }
-    if (cudaStreamSynchronize(s->stream) != cudaSuccess) {
-        cudaFree(d_tmp);
-        return ARK_E_CUDA;
-    }
-    int all_ok = 0;
-    cudaMemcpy(&all_ok, d_ok, sizeof(int), cudaMemcpyDeviceToHost);
-    cudaFree(d_tmp);
-    s->p2p = all_ok != 0;
+    s->p2p = all_ok;
     return ARK_OK;
 }
 
@@ -588,6 +755,17 @@ void teardown_p2p(ark_opt_state* s) {
     s->d_peers = nullptr;
     s->xchg = nullptr;
     s->p2p = false;
+}
+
+void teardown_grads(ark_opt_state* s) {
+    for (size_t r = 0; r < s->gpeer.size(); ++r)
+        if (s->gpeer[r] && s->gpeer[r] != s->gbuf) cudaIpcCloseMemHandle(s->gpeer[r]);
+    s->gpeer.clear();
+    if (s->d_gsrc) cudaFree(s->d_gsrc);
+    if (s->gbuf) cudaFree(s->gbuf);
+    s->d_gsrc = nullptr;
+    s->gbuf = nullptr;
+    s->gbuf_n = 0;
 }
 
 StepParams make_params(const ark_opt_state* s, const uint16_t* g16) {
@@ -620,6 +798,8 @@ StepParams make_params(const ark_opt_state* s, const uint16_t* g16) {
     p.xchg = s->xchg;
     p.peers = s->d_peers;
     p.peer_timeout_ns = s->timeout_ns;
+    p.gsrc = s->d_gsrc;
+    p.g16_out = nullptr;
     p.blk_sum = s->d_blk_sum;
     p.blk_bad = s->d_blk_bad;
     p.ticket1 = s->d_tickets;
@@ -637,10 +817,12 @@ StepParams make_params(const ark_opt_state* s, const uint16_t* g16) {
                            : cudaEventRecord((e), (st)))
 
 int enqueue_step(ark_opt_state* s, cudaStream_t stream, uint16_t* w16, const uint16_t* g16,
-                 float* m, float* v, cudaEvent_t* ev, bool capturing = false) {
+                 float* m, float* v, cudaEvent_t* ev, bool capturing = false, bool reduce = false) {
     StepParams p = make_params(s, g16);
+    if (reduce) p.g16_out = const_cast<uint16_t*>(g16);
     if (ev) ARK_RECORD(ev[0], stream);
-    s->pass1<<<s->blocks1, kThreads, 0, stream>>>(p);
+    if (reduce) kPass1Reduce<<<s->blocks1r, kThreads, 0, stream>>>(p);
+    else s->pass1<<<s->blocks1, kThreads, 0, stream>>>(p);
     ARK_CUDA_TRY(cudaGetLastError());
     if (ev) ARK_RECORD(ev[1], stream);
     if (s->cfg.world_size > 1 && !s->p2p) {
@@ -669,17 +851,18 @@ void drop_graph(ark_opt_state* s, int slot) {
 // on placeholder events, whose nodes are then located for retargeting).
 int capture_graph(ark_opt_state* s, int slot, uint16_t* w16, const uint16_t* g16, float* m,
                   float* v) {
+    const bool profiled = slot & 1, reduce = slot >= 2;
     drop_graph(s, slot);
     // capture on a private stream (the legacy default stream cannot be
     // captured); the graph is then launched on the state's stream
     if (!s->capture_stream)
         ARK_CUDA_TRY(cudaStreamCreateWithFlags(&s->capture_stream, cudaStreamNonBlocking));
-    if (slot == 1 && !s->ph_ev[0])
+    if (profiled && !s->ph_ev[0])
         for (auto& e : s->ph_ev) ARK_CUDA_TRY(cudaEventCreate(&e));
     cudaGraph_t g = nullptr;
     ARK_CUDA_TRY(cudaStreamBeginCapture(s->capture_stream, cudaStreamCaptureModeThreadLocal));
-    const int rc =
-        enqueue_step(s, s->capture_stream, w16, g16, m, v, slot ? s->ph_ev : nullptr, true);
+    const int rc = enqueue_step(s, s->capture_stream, w16, g16, m, v,
+                                profiled ? s->ph_ev : nullptr, true, reduce);
     const cudaError_t e = cudaStreamEndCapture(s->capture_stream, &g);
     if (rc != ARK_OK) {
         if (g) cudaGraphDestroy(g);
@@ -687,7 +870,8 @@ int capture_graph(ark_opt_state* s, int slot, uint16_t* w16, const uint16_t* g16
     }
     ARK_CUDA_TRY(e);
     s->gsrc[slot] = g;
-    if (slot == 1) {
+    if (profiled) {
+        cudaGraphNode_t* evn = s->ev_node[slot >> 1];
         size_t nn = 0;
         ARK_CUDA_TRY(cudaGraphGetNodes(g, nullptr, &nn));
         std::vector<cudaGraphNode_t> nodes(nn);
@@ -699,10 +883,10 @@ int capture_graph(ark_opt_state* s, int slot, uint16_t* w16, const uint16_t* g16
             cudaEvent_t ev = nullptr;
             ARK_CUDA_TRY(cudaGraphEventRecordNodeGetEvent(node, &ev));
             for (int j = 0; j < 4; ++j)
-                if (ev == s->ph_ev[j]) s->ev_node[j] = node;
+                if (ev == s->ph_ev[j]) evn[j] = node;
         }
         for (int j = 0; j < 4; ++j)
-            if (!s->ev_node[j]) return ARK_E_CUDA;
+            if (!evn[j]) return ARK_E_CUDA;
     }
     ARK_CUDA_TRY(cudaGraphInstantiate(&s->gexec[slot], g, 0));
     const void* key[4] = {w16, g16, m, v};
@@ -756,11 +940,13 @@ int ark_cuda_opt_init(const ark_opt_cfg* cfg, ark_opt_state** out) {
     if (const char* e = getenv("ARK_PASS2_VARIANT")) var2 = atoi(e);
     if (var2 < 0 || var2 >= (int)(sizeof(kPass2Variants) / sizeof(kPass2Variants[0]))) var2 = 0;
     s->pass2 = kPass2Variants[var2].fn;
+    s->blocks1r = streaming_grid(reinterpret_cast<const void*>(kPass1Reduce), kThreads, 0,
+                                 (cfg->n >> 3) / 2 + 1);
     s->blocks2 = streaming_grid(reinterpret_cast<const void*>(s->pass2), kThreads, 0,
                                 (cfg->n >> 3) / kPass2Variants[var2].unroll + 1);
     const int W = cfg->world_size;
     s->timeout_ns = (uint64_t)(cfg->wait_timeout_ms ? cfg->wait_timeout_ms : 5000u) * 1000000ull;
-    const int nblk = s->blocks1;
+    const int nblk = s->blocks1 > s->blocks1r ? s->blocks1 : s->blocks1r;
     // carve one allocation: state | lr table | block partials | tickets | partials
     size_t off = 0;
     auto take = [&](size_t bytes) {
@@ -821,20 +1007,26 @@ int ark_cuda_opt_init(const ark_opt_cfg* cfg, ark_opt_state** out) {
     return ARK_OK;
 }
 
-int ark_cuda_opt_step(ark_opt_state* s, uint16_t* w16, const uint16_t* g16, float* m, float* v) {
+static int run_step(ark_opt_state* s, uint16_t* w16, const uint16_t* g16, float* m, float* v,
+                    bool reduce) {
     if (!s) return ARK_E_INVALID_ARG;
     if (s->cfg.n && (!w16 || !g16 || !m || !v)) return ARK_E_INVALID_ARG;
     if (!aligned16(w16) || !aligned16(g16) || !aligned16(m) || !aligned16(v))
         return ARK_E_MISALIGNED;
+    if (reduce) {
+        if (!s->gbuf) return ARK_E_INVALID_ARG;          // no ark_cuda_opt_grad_buffer yet
+        if (s->cfg.shard_offset + s->cfg.n > s->gbuf_n) return ARK_E_INVALID_ARG;
+        if ((s->cfg.shard_offset & 7u) != 0) return ARK_E_MISALIGNED;
+    }
     DeviceGuard dg(s->device);
     const bool profile = s->prof_used < s->prof_cap;
     cudaEvent_t* ev = profile ? &s->prof_events[4 * s->prof_used] : nullptr;
     if (!(s->cfg.flags & ARK_OPT_USE_GRAPH)) {
-        const int rc = enqueue_step(s, s->stream, w16, g16, m, v, ev);
+        const int rc = enqueue_step(s, s->stream, w16, g16, m, v, ev, false, reduce);
         if (rc == ARK_OK && profile) s->prof_used++;
         return rc;
     }
-    const int slot = profile ? 1 : 0;
+    const int slot = (reduce ? 2 : 0) + (profile ? 1 : 0);
     const void* key[4] = {w16, g16, m, v};
     if (!s->gexec[slot] || memcmp(key, s->gkey[slot], sizeof(key)) != 0) {
         const int rc = capture_graph(s, slot, w16, g16, m, v);
@@ -845,9 +1037,55 @@ int ark_cuda_opt_step(ark_opt_state* s, uint16_t* w16, const uint16_t* g16, floa
     }
     if (profile)   // this replay records into this step's profiling events
         for (int j = 0; j < 4; ++j)
-            ARK_CUDA_TRY(cudaGraphExecEventRecordNodeSetEvent(s->gexec[1], s->ev_node[j], ev[j]));
+            ARK_CUDA_TRY(cudaGraphExecEventRecordNodeSetEvent(s->gexec[slot],
+                                                              s->ev_node[slot >> 1][j], ev[j]));
     ARK_CUDA_TRY(cudaGraphLaunch(s->gexec[slot], s->stream));
     if (profile) s->prof_used++;
+    return ARK_OK;
+}
+
+int ark_cuda_opt_step(ark_opt_state* s, uint16_t* w16, const uint16_t* g16, float* m, float* v) {
+    return run_step(s, w16, g16, m, v, false);
+}
+
+int ark_cuda_opt_step_reduce(ark_opt_state* s, uint16_t* w16, uint16_t* g16_shard, float* m,
+                             float* v) {
+    return run_step(s, w16, g16_shard, m, v, true);
+}
+
+int ark_cuda_opt_grad_buffer(ark_opt_state* s, uint64_t n_full, uint16_t** out) {
+    if (!s || !out || n_full == 0) return ARK_E_INVALID_ARG;
+    *out = nullptr;
+    if (s->cfg.shard_offset + s->cfg.n > n_full) return ARK_E_INVALID_ARG;
+    const int W = s->cfg.world_size;
+    if (W > 1 && !s->p2p) return ARK_E_UNSUPPORTED;      // needs the mapped exchange slots
+    DeviceGuard dg(s->device);
+    teardown_grads(s);
+    const size_t bytes = ((n_full * sizeof(uint16_t)) + 255) & ~size_t(255);
+    if (cudaMalloc(&s->gbuf, bytes) != cudaSuccess) {
+        s->gbuf = nullptr;
+        if (W == 1) return ARK_E_CUDA;
+    } else if (cudaMemset(s->gbuf, 0, bytes) != cudaSuccess) {
+        return ARK_E_CUDA;
+    }
+    if (W == 1) {
+        s->gpeer.assign(1, s->gbuf);
+    } else {
+        bool all_ok = false;
+        const int rc = share_ipc(s, s->gbuf, s->gpeer, &all_ok);
+        if (rc || !all_ok) {
+            teardown_grads(s);
+            return rc ? rc : ARK_E_UNSUPPORTED;
+        }
+    }
+    if (cudaMalloc(&s->d_gsrc, sizeof(uint16_t*) * W) != cudaSuccess ||
+        cudaMemcpy(s->d_gsrc, s->gpeer.data(), sizeof(uint16_t*) * W, cudaMemcpyHostToDevice) !=
+            cudaSuccess) {
+        teardown_grads(s);
+        return ARK_E_CUDA;
+    }
+    s->gbuf_n = n_full;
+    *out = static_cast<uint16_t*>(s->gbuf);
     return ARK_OK;
 }
 
@@ -943,8 +1181,8 @@ int ark_cuda_opt_destroy(ark_opt_state* s) {
     if (!s) return ARK_OK;
     DeviceGuard dg(s->device);
     cudaStreamSynchronize(s->stream);
-    drop_graph(s, 0);
-    drop_graph(s, 1);
+    for (int slot = 0; slot < 4; ++slot) drop_graph(s, slot);
+    teardown_grads(s);
     for (cudaEvent_t e : s->ph_ev)
         if (e) cudaEventDestroy(e);
     if (s->capture_stream) cudaStreamDestroy(s->capture_stream);

@@ -172,6 +172,33 @@ class Optimizer:
                                  _ptr(m, "f32", self.n), _ptr(v, "f32", self.n))
         _lib.check("ark_cuda_opt_step", rc)
 
+    def grad_buffer(self, n_full: int | None = None):
+        """This rank's full gradient buffer for step_reduce (FP16, all
+        n_full global elements, zeroed), as a CUDA tensor over library
+        memory.  Collective: every rank calls it."""
+        import torch
+        n_full = self.layout.n if n_full is None else int(n_full)
+        p = ctypes.c_void_p()
+        _lib.check("ark_cuda_opt_grad_buffer",
+                   _lib.lib().ark_cuda_opt_grad_buffer(self._h, n_full, ctypes.byref(p)))
+
+        class _View:
+            __cuda_array_interface__ = {"shape": (n_full,), "typestr": "<f2",
+                                        "data": (p.value, False), "version": 3,
+                                        "strides": None}
+
+        self._gbuf = torch.as_tensor(_View(), device=torch.device("cuda", self._cfg.device))
+        return self._gbuf
+
+    def step_reduce(self, w16, g16_shard, m, v):
+        """One step on the sum over ranks of every rank's grad_buffer():
+        the gradient hand-off fused with pass 1 (peer reads over NVLink);
+        the reduced FP16 shard is written to g16_shard."""
+        rc = _lib.lib().ark_cuda_opt_step_reduce(
+            self._h, _ptr(w16, "f16", self.n), _ptr(g16_shard, "f16", self.n),
+            _ptr(m, "f32", self.n), _ptr(v, "f32", self.n))
+        _lib.check("ark_cuda_opt_step_reduce", rc)
+
     def upload_grads(self, g16_dev, g16_host):
         """Asynchronous H2D copy of this shard's scaled grads (host tensor or
         numpy array; pinned memory for full speed)."""

@@ -299,6 +299,17 @@ def run_ours(args):
                        use_graph=args.graph, nccl_exchange=args.nccl_exchange)
     lo, n = opt.lo, opt.n
     w16, g16, m, v = synth.make_state(n, lo, SEED, dev, loss_scale=LOSS_SCALE, heavy=heavy)
+    if args.reduce:
+        # gradient hand-off: each rank's full FP16 gradients (its own backward
+        # output, scaled 1/world so the sum has the usual magnitude)
+        full = opt.grad_buffer()
+        synth.fill_grads(full, 0, SEED + 1 + rank, LOSS_SCALE / world, heavy=heavy)
+
+        def do_step():
+            opt.step_reduce(w16, g16, m, v)
+    else:
+        def do_step():
+            opt.step_all(w16, g16, m, v)
     torch.cuda.synchronize()
 
     def barrier():
@@ -317,7 +328,7 @@ def run_ours(args):
     sampled = list(range(world)) if rank == 0 else [local]
     with ClockSampler(nvidia_smi_ids(sampled)) as clocks:
         for _ in range(args.warmup):
-            opt.step_all(w16, g16, m, v)
+            do_step()
         torch.cuda.synchronize()
         opt.profile_begin(args.steps)
         barrier()
@@ -325,7 +336,7 @@ def run_ours(args):
         clocks.mark("t0")
         ev0.record(stream)
         for _ in range(args.steps):
-            opt.step_all(w16, g16, m, v)
+            do_step()
         ev1.record(stream)
         torch.cuda.synchronize()
         clocks.mark("t1")
@@ -372,6 +383,13 @@ def run_ours(args):
                 "pass1_ms": round(p1, 4),
                 "pass1_gbs": round(PASS1_BYTES_PER_PARAM * n / (p1 * 1e-3) / 1e9, 1),
                 "exchange_ms": round(ex, 4), "launches_per_step": 2}
+        if args.reduce:
+            # pass 1 here is the reduce-scatter fused with the norm/flag pass:
+            # every rank reads (world - 1) remote shards over NVLink
+            roof["pass1_kernel"] = "ark::pass1_reduce_kernel (reduce-scatter over NVLink + norm/flag)"
+            roof["nvlink_bytes_in_per_gpu"] = 2 * n * (world - 1)
+            roof["nvlink_gbs_in_per_gpu"] = round(2 * n * (world - 1) / (p1 * 1e-3) / 1e9, 1)
+            roof["nvlink_peer_copy_gbs_measured"] = 770.0
     clk = clocks.summary()
     geom = opt.geometry()
 
@@ -389,7 +407,8 @@ def run_ours(args):
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded splitmix64 + Irwin-Hall normals with the BASELINE "
                     "distributions, generated on the device)",
-            "config": {"workload": workload,
+            "config": {"workload": workload + (" + gradient hand-off (reduce-scatter over NVLink "
+                                               "fused with pass 1)" if args.reduce else ""),
                        "params": L.n, "params_per_gpu": n, "tensors": L.n_tensors,
                        "parallelism": f"zero1-dp{world}", "t": START_STEP,
                        "loss_scale": LOSS_SCALE, "clip": "active",
@@ -425,6 +444,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--params", type=int, default=0,
                     help="flat-buffer workload of this many params instead of EKO-237M")
+    ap.add_argument("--reduce", action="store_true",
+                    help="include the gradient hand-off: reduce-scatter of every rank's full "
+                         "FP16 gradients over NVLink, fused with pass 1")
     ap.add_argument("--workload", choices=("eko", "1.3b", "7b"), default="eko",
                     help="model layout (BASELINE configs 0, 2, 3); the headline is eko")
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")

@@ -204,6 +204,26 @@ ARK_API int ark_cuda_opt_init(const ark_opt_cfg* cfg, ark_opt_state** out);
 ARK_API int ark_cuda_opt_step(ark_opt_state* st, uint16_t* w16, const uint16_t* g16, float* m,
                       float* v);
 
+/* The gradient hand-off, for data-parallel ranks: allocate this rank's
+ * FULL gradient buffer (n_full FP16 loss-scaled elements, all global
+ * indices, zeroed), map every rank's buffer into every other rank
+ * (collective: every rank calls it; needs the peer-to-peer exchange slots
+ * when world_size > 1).  The backward writes each rank's own gradients
+ * there; the library owns the buffer until ark_cuda_opt_destroy. */
+ARK_API int ark_cuda_opt_grad_buffer(ark_opt_state* st, uint64_t n_full, uint16_t** g16_full);
+
+/* One optimizer step on the SUM over ranks of every rank's full gradient
+ * buffer: replaces the reference's zero-then-accumulate of the backward's
+ * gradients (src/memory.rs:338-342, objc/bridge.m:907-949) followed by the
+ * optimizer block.  Pass 1 reads this rank's shard range from every rank's
+ * buffer over NVLink, sums the FP16 values in FP32 in rank order, rounds
+ * once to FP16 into g16_shard (cfg.n elements, this device) and checks /
+ * squares the result; pass 2 is the ordinary update.  Each rank's buffer
+ * may be overwritten once this step has completed on its stream.
+ * cfg.shard_offset must be a multiple of 8. */
+ARK_API int ark_cuda_opt_step_reduce(ark_opt_state* st, uint16_t* w16, uint16_t* g16_shard,
+                                     float* m, float* v);
+
 /* Wait for the state's stream and copy the device state out.  Returns
  * ARK_E_EARLY_STOP once the early-stop condition holds (training.rs:298),
  * a device error code if one was raised, else ARK_OK. */

@@ -363,6 +363,20 @@ ORK_API int ork_step_flat_f16(const ork_step_cfg* cfg, ork_amp_state* st,
     return ork_apply_f16(cfg, st, w16, g16, m, v, n, 0, s, bad);
 }
 
+/* Gradient hand-off for data-parallel ranks: this rank's shard of the sum
+ * over ranks of every rank's full FP16 gradients, accumulated in f32 in rank
+ * order from 0 (the reference's zero-then-+= accumulation, memory.rs:338-342,
+ * bridge.m:907-949, applied once per rank) and rounded once to FP16. */
+ORK_API void ork_reduce_f16(const uint16_t* const* srcs, int nranks, uint64_t n,
+                            uint64_t offset, uint16_t* out) {
+    #pragma omp parallel for schedule(static)
+    for (int64_t ii = 0; ii < (int64_t)n; ++ii) {
+        float acc = 0.0f;
+        for (int r = 0; r < nranks; ++r) acc = acc + ork_h2f(srcs[r][offset + (uint64_t)ii]);
+        out[ii] = ork_f2h(acc);
+    }
+}
+
 /* Warmup + cosine schedule, optimizer.rs:80-92, in f32 (cosf from libm). */
 ORK_API float ork_lr_now(float lr, uint32_t warmup, uint32_t step) {
     if (step < warmup) return lr * ((float)step + 1.0f) / (float)warmup;

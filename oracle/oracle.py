@@ -74,6 +74,7 @@ def lib():
             "ork_step_flat_f16": (c_i, [ctypes.POINTER(StepCfg), ctypes.POINTER(AmpState), c_p, c_p,
                                         c_p, c_p, c_u64]),
             "ork_lr_now": (c_f, [c_f, c_u32, c_u32]),
+            "ork_reduce_f16": (None, [ctypes.POINTER(c_p), c_i, c_u64, c_u64, c_p]),
             "ork_ref_step_tensors": (c_i, [ctypes.POINTER(Tensor), c_i, ctypes.POINTER(AmpState), c_f,
                                            c_f, c_f, c_f, c_f, c_f, c_u32, c_i]),
             "ork_max_threads": (c_i, []),
@@ -176,6 +177,15 @@ def apply_f16(cfg, st, w16, g16, m, v, offset, sumsq, nonfinite):
 def step_flat_f16(cfg, st, w16, g16, m, v):
     return lib().ork_step_flat_f16(ctypes.byref(cfg), ctypes.byref(st), ptr(w16), ptr(g16),
                                    ptr(m), ptr(v), len(g16))
+
+
+def reduce_f16(srcs, n, offset):
+    """Shard [offset, offset+n) of the rank-ordered f32 sum of FP16 buffers."""
+    srcs = [np.ascontiguousarray(x, np.uint16) for x in srcs]
+    arr = (c_p * len(srcs))(*[x.ctypes.data for x in srcs])
+    out = np.empty(n, np.uint16)
+    lib().ork_reduce_f16(arr, len(srcs), n, offset, ptr(out))
+    return out
 
 
 def synth_f16(n, offset, seed, stream, sigma, mult=1.0, heavy_every=0, heavy_mult=1.0):

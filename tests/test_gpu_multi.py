@@ -185,3 +185,93 @@ def test_peer_wait_times_out_when_a_rank_leaves():
     assert rc0 == 0 and step0 == 1 and res[1] == (0, 1)
     assert rc1 == -5 and err == -5           # ARK_E_TIMEOUT, step skipped
     assert step_after == 1 and x == 1024.0
+
+
+def _reduce_rank_main(rank, world, port, q):
+    import datetime
+
+    import torch.distributed as dist
+
+    import ark_b200 as ab
+    from ark_b200 import dist as adist
+    from ark_b200 import layout, synth
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    comm = adist.nccl_comm(rank, world, rank)
+    try:
+        L = layout.decoder_layout("multi", 4, 96, 256, 1000)
+        adam = ab.AdamConfig(lr=3e-4, beta1=0.9, beta2=0.95, eps=1e-8, weight_decay=0.1,
+                             grad_clip=1.0)
+        sc = ab.LossScaleConfig(init=4096.0, every=2, max=2.0 ** 24)
+        opt = ab.Optimizer(L, adam, sc, device=rank, rank=rank, world=world, comm=comm,
+                           constant_lr=True, initial_step=999)
+        lo, hi, n = opt.lo, opt.hi, opt.n
+        w16, _, m, v = synth.make_state(n, lo, 91, "cuda", loss_scale=4096.0)
+        full = opt.grad_buffer()
+        shard_g = torch.zeros(n, dtype=torch.float16, device="cuda")
+        statuses, shards = [], []
+        for k in range(1, 5):
+            # this rank's backward output for step k (stream 0x400 + 16 k + rank)
+            synth.fill_f16(full, 0, 91, 0x400 + 16 * k + rank, 1e-3, mult=4096.0)
+            if k == 2 and rank == world - 1:
+                full.view(torch.int16)[L.n // 2] = 0x7E00
+            opt.step_reduce(w16, shard_g, m, v)
+            statuses.append(opt.status())
+            shards.append(shard_g.cpu().numpy().view(np.uint16).copy())
+        q.put((rank, lo, hi, w16.cpu().numpy().view(np.uint16), m.cpu().numpy(),
+               v.cpu().numpy(), statuses, shards))
+        opt.close()
+    finally:
+        adist.nccl_comm_destroy(comm)
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason="needs 2 GPUs")
+@pytest.mark.parametrize("world", WORLDS)
+def test_reduce_scatter_step_matches_oracle(oracle, world):
+    """The gradient hand-off fused with pass 1: every rank reads its shard of
+    every rank's full gradient buffer over NVLink and sums in rank order."""
+    from ark_b200 import layout, synth
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_reduce_rank_main, args=(r, world, port, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    res = sorted([q.get(timeout=300) for _ in range(world)], key=lambda r: r[0])
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    L = layout.decoder_layout("multi", 4, 96, 256, 1000)
+    n = L.n
+    w = oracle.synth_f16(n, 0, 91, synth.STREAM_W, 0.02)
+    m = oracle.synth_f32(n, 0, 91, synth.STREAM_M, 1e-4)
+    v = oracle.synth_f32(n, 0, 91, synth.STREAM_V, 1e-3, square=True)
+    cfg = oracle.make_cfg(n_decay=L.n_decay, scale_every=2, scale_max=2.0 ** 24)
+    st = oracle.make_state(4096.0, opt_step=999)
+    ref_states, ref_shards = [], []
+    for k in range(1, 5):
+        fulls = [oracle.synth_f16(n, 0, 91, 0x400 + 16 * k + r, 1e-3, 4096.0)
+                 for r in range(world)]
+        if k == 2:
+            fulls[world - 1][n // 2] = 0x7E00
+        g = oracle.reduce_f16(fulls, n, 0)
+        ref_shards.append(g)
+        s, bad = oracle.partial_f16(cfg, st, g, 0)
+        oracle.apply_f16(cfg, st, w, g, m, v, 0, s, bad)
+        ref_states.append((st.loss_scale, st.opt_step, st.last_overflow, st.clean_steps))
+    for rank, lo, hi, ws, ms, vs, sts, shards in res:
+        for k in range(4):
+            assert np.array_equal(shards[k], ref_shards[k][lo:hi]), (rank, k)
+            s = sts[k]
+            assert (s["loss_scale"], s["opt_step"], s["last_overflow"], s["clean_steps"]) == \
+                ref_states[k], (rank, k)
+        assert np.array_equal(ws, w[lo:hi]), rank
+        assert np.array_equal(ms.view(np.uint32), m[lo:hi].view(np.uint32)), rank
+        assert np.array_equal(vs.view(np.uint32), v[lo:hi].view(np.uint32)), rank

@@ -207,3 +207,36 @@ def test_profile_events(use_graph):
         opt.step_all(*bufs)
     assert opt.status()["steps_called"] == 5
     opt.close()
+
+
+@pytest.mark.parametrize("shard", [None, (1024, 8232)])
+def test_reduce_step_single_rank(oracle, shard):
+    """step_reduce on one rank: the shard of the (one-rank) sum of the full
+    gradient buffer, then the ordinary step, against the oracle."""
+    L = tiny()
+    adam = ab.AdamConfig(lr=3e-4, beta1=0.9, beta2=0.95, eps=1e-8, weight_decay=0.1,
+                         grad_clip=1.0)
+    sc = ab.LossScaleConfig(init=65536.0, every=50, max=2.0 ** 24)
+    opt = ab.Optimizer(L, adam, sc, constant_lr=True, initial_step=999, shard=shard)
+    lo, n = opt.lo, opt.n
+    full = opt.grad_buffer()
+    assert full.numel() == L.n and int(full.view(torch.int16).abs().sum()) == 0
+    w, _, m, v = oracle_bufs(oracle, n, lo, SEED, 65536.0)
+    dw, dm, dv = dev(w), dev(m), dev(v)
+    shard_g = torch.zeros(n, dtype=torch.float16, device="cuda")
+    cfg = oracle.make_cfg(n_decay=L.n_decay, scale_every=50, scale_max=2.0 ** 24)
+    ost = oracle.make_state(65536.0, opt_step=999)
+    for k in range(1, 4):
+        synth.fill_f16(full, 0, SEED, 0x300 + k, 1e-3, mult=65536.0)
+        g_full = oracle.synth_f16(L.n, 0, SEED, 0x300 + k, 1e-3, 65536.0)
+        if k == 2:
+            full.view(torch.int16)[lo + 5] = 0x7C00
+            g_full[lo + 5] = 0x7C00
+        opt.step_reduce(dw, shard_g, dm, dv)
+        g = oracle.reduce_f16([g_full], n, lo)
+        assert np.array_equal(host(shard_g), g)
+        s, bad = oracle.partial_f16(cfg, ost, g, lo)
+        oracle.apply_f16(cfg, ost, w, g, m, v, lo, s, bad)
+        check_state(opt.status(), ost, f"step {k}")
+    assert same_f16(host(dw), w) and same_f32(host(dm), m) and same_f32(host(dv), v)
+    opt.close()
