@@ -25,6 +25,7 @@ ARK_COMPAT_CLIP_NEON_FOLD = 0x1
 ARK_OPT_COMPAT_GAMMA_FINAL_UNSCALED = 0x1
 ARK_OPT_USE_GRAPH = 0x2
 ARK_OPT_NCCL_EXCHANGE = 0x4
+ARK_STEP_REDUCE = 0x1
 
 c_f, c_u32, c_u64, c_i, c_i32, c_d, c_p = (ctypes.c_float, ctypes.c_uint32, ctypes.c_uint64,
                                            ctypes.c_int, ctypes.c_int32, ctypes.c_double,
@@ -77,6 +78,7 @@ SIGNATURES = {
     "ark_cuda_opt_step": (c_i, [c_p, c_p, c_p, c_p, c_p]),
     "ark_cuda_opt_grad_buffer": (c_i, [c_p, c_u64, ctypes.POINTER(c_p)]),
     "ark_cuda_opt_step_reduce": (c_i, [c_p, c_p, c_p, c_p, c_p]),
+    "ark_cuda_opt_step_ex": (c_i, [c_p, c_p, c_p, c_p, c_p, c_p, c_u32]),
     "ark_cuda_opt_read_status": (c_i, [c_p, ctypes.POINTER(OptStatus)]),
     "ark_cuda_opt_set_status": (c_i, [c_p, ctypes.POINTER(OptStatus)]),
     "ark_cuda_opt_upload_grads": (c_i, [c_p, c_p, c_p, c_u64]),

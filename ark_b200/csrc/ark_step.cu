@@ -71,6 +71,7 @@ struct StepParams {
     // reduce-scatter step: every rank's full FP16 gradient buffer (mapped here)
     const uint16_t* const* gsrc;
     uint16_t* g16_out;               // this rank's reduced shard
+    float* w32_out;                  // optional FP32 copy of the updated weights
 };
 
 constexpr int kThreads = 256;
@@ -498,7 +499,7 @@ __device__ __forceinline__ void update8(uint4& wq, const uint4 gq, float4& m0, f
 // Grid-stride over 8-element vectors in reverse (vector i = nvec-1-j for the
 // j-th in forward order): consecutive threads still touch consecutive
 // vectors, and the first vectors updated are the last ones pass 1 read.
-template <int kUnroll2, int MINB>
+template <int kUnroll2, int MINB, bool kW32>
 __global__ void __launch_bounds__(kThreads, MINB) pass2_kernel(StepParams p,
                                                               uint16_t* __restrict__ w16,
                                                               float* __restrict__ m,
@@ -539,6 +540,13 @@ __global__ void __launch_bounds__(kThreads, MINB) pass2_kernel(StepParams p,
                     const uint64_t i = nvec - 1 - j;
                     update8(wq[u], gq[u], ma[u], mb[u], va[u], vb[u], p.offset + (i << 3), pl, p);
                     st_stream(w4 + i, wq[u]);
+                    if (kW32) {   // the forward's FP32 weights (training.rs:165-186)
+                        float4* o = reinterpret_cast<float4*>(p.w32_out) + 2 * i;
+                        st_stream(o, make_float4(h2f(lo16(wq[u].x)), h2f(hi16(wq[u].x)),
+                                                 h2f(lo16(wq[u].y)), h2f(hi16(wq[u].y))));
+                        st_stream(o + 1, make_float4(h2f(lo16(wq[u].z)), h2f(hi16(wq[u].z)),
+                                                     h2f(lo16(wq[u].w)), h2f(hi16(wq[u].w))));
+                    }
                     st_stream(m4 + 2 * i, ma[u]);
                     st_stream(m4 + 2 * i + 1, mb[u]);
                     st_stream(v4 + 2 * i, va[u]);
@@ -555,6 +563,7 @@ __global__ void __launch_bounds__(kThreads, MINB) pass2_kernel(StepParams p,
             const float decay = gi < p.n_decay ? pl.k.decay : 1.0f;
             float mi = m[i], vi = v[i];
             w16[i] = f2h(adam_elem(h2f(w16[i]), gf, mi, vi, pl.k, decay));
+            if (kW32) p.w32_out[i] = h2f(w16[i]);
             m[i] = mi;
             v[i] = vi;
         }
@@ -572,7 +581,7 @@ struct Pass1Variant {
 };
 struct Pass2Variant {
     int unroll, min_blocks;
-    Pass2Fn fn;
+    Pass2Fn fn, fn_w32;    // plain / also writing the FP32 weight copy
 };
 static const Pass1Variant kPass1Variants[] = {
     {4, 4, pass1_kernel<4, 4>},
@@ -583,10 +592,10 @@ static const Pass1Variant kPass1Variants[] = {
 };
 static const Pass1Fn kPass1Reduce = pass1_reduce_kernel<2, 4>;
 static const Pass2Variant kPass2Variants[] = {
-    {2, 1, pass2_kernel<2, 1>},
-    {1, 3, pass2_kernel<1, 3>},
-    {1, 4, pass2_kernel<1, 4>},
-    {3, 1, pass2_kernel<3, 1>},
+    {2, 1, pass2_kernel<2, 1, false>, pass2_kernel<2, 1, true>},
+    {1, 3, pass2_kernel<1, 3, false>, pass2_kernel<1, 3, true>},
+    {1, 4, pass2_kernel<1, 4, false>, pass2_kernel<1, 4, true>},
+    {3, 1, pass2_kernel<3, 1, false>, pass2_kernel<3, 1, true>},
 };
 
 }  // namespace ark
@@ -613,7 +622,8 @@ struct ark_opt_state {
     ark_opt_status* h_status = nullptr;  // pinned
     int blocks1 = 0, blocks2 = 0, blocks1r = 0;
     Pass1Fn pass1 = nullptr;                  // chosen launch-shape variants
-    Pass2Fn pass2 = nullptr;
+    Pass2Fn pass2 = nullptr, pass2_w32 = nullptr;
+    int blocks2w = 0;
     // P2P exchange slots (world > 1)
     bool p2p = false;
     uint64_t* xchg = nullptr;                 // own receive slots (cudaMalloc, IPC-exported)
@@ -631,7 +641,7 @@ struct ark_opt_state {
     // (slots 2 and 3: the same for the reduce-scatter step)
     cudaGraph_t gsrc[4] = {nullptr, nullptr, nullptr, nullptr};
     cudaGraphExec_t gexec[4] = {nullptr, nullptr, nullptr, nullptr};
-    const void* gkey[4][4] = {};
+    const void* gkey[4][5] = {};
     cudaGraphNode_t ev_node[2][4] = {};     // per profiled slot (1, 3)
     cudaEvent_t ph_ev[4] = {nullptr, nullptr, nullptr, nullptr};   // capture placeholders
     cudaStream_t capture_stream = nullptr;
@@ -800,6 +810,7 @@ StepParams make_params(const ark_opt_state* s, const uint16_t* g16) {
     p.peer_timeout_ns = s->timeout_ns;
     p.gsrc = s->d_gsrc;
     p.g16_out = nullptr;
+    p.w32_out = nullptr;
     p.blk_sum = s->d_blk_sum;
     p.blk_bad = s->d_blk_bad;
     p.ticket1 = s->d_tickets;
@@ -817,9 +828,11 @@ StepParams make_params(const ark_opt_state* s, const uint16_t* g16) {
                            : cudaEventRecord((e), (st)))
 
 int enqueue_step(ark_opt_state* s, cudaStream_t stream, uint16_t* w16, const uint16_t* g16,
-                 float* m, float* v, cudaEvent_t* ev, bool capturing = false, bool reduce = false) {
+                 float* m, float* v, float* w32, cudaEvent_t* ev, bool capturing = false,
+                 bool reduce = false) {
     StepParams p = make_params(s, g16);
     if (reduce) p.g16_out = const_cast<uint16_t*>(g16);
+    p.w32_out = w32;
     if (ev) ARK_RECORD(ev[0], stream);
     if (reduce) kPass1Reduce<<<s->blocks1r, kThreads, 0, stream>>>(p);
     else s->pass1<<<s->blocks1, kThreads, 0, stream>>>(p);
@@ -834,7 +847,8 @@ int enqueue_step(ark_opt_state* s, cudaStream_t stream, uint16_t* w16, const uin
         }
     }
     if (ev) ARK_RECORD(ev[2], stream);
-    s->pass2<<<s->blocks2, kThreads, 0, stream>>>(p, w16, m, v);
+    if (w32) s->pass2_w32<<<s->blocks2w, kThreads, 0, stream>>>(p, w16, m, v);
+    else s->pass2<<<s->blocks2, kThreads, 0, stream>>>(p, w16, m, v);
     ARK_CUDA_TRY(cudaGetLastError());
     if (ev) ARK_RECORD(ev[3], stream);
     return ARK_OK;
@@ -850,7 +864,7 @@ void drop_graph(ark_opt_state* s, int slot) {
 // Capture one step into graph slot 0 (plain) or 1 (with event-record nodes
 // on placeholder events, whose nodes are then located for retargeting).
 int capture_graph(ark_opt_state* s, int slot, uint16_t* w16, const uint16_t* g16, float* m,
-                  float* v) {
+                  float* v, float* w32) {
     const bool profiled = slot & 1, reduce = slot >= 2;
     drop_graph(s, slot);
     // capture on a private stream (the legacy default stream cannot be
@@ -861,7 +875,7 @@ int capture_graph(ark_opt_state* s, int slot, uint16_t* w16, const uint16_t* g16
         for (auto& e : s->ph_ev) ARK_CUDA_TRY(cudaEventCreate(&e));
     cudaGraph_t g = nullptr;
     ARK_CUDA_TRY(cudaStreamBeginCapture(s->capture_stream, cudaStreamCaptureModeThreadLocal));
-    const int rc = enqueue_step(s, s->capture_stream, w16, g16, m, v,
+    const int rc = enqueue_step(s, s->capture_stream, w16, g16, m, v, w32,
                                 profiled ? s->ph_ev : nullptr, true, reduce);
     const cudaError_t e = cudaStreamEndCapture(s->capture_stream, &g);
     if (rc != ARK_OK) {
@@ -889,7 +903,7 @@ int capture_graph(ark_opt_state* s, int slot, uint16_t* w16, const uint16_t* g16
             if (!evn[j]) return ARK_E_CUDA;
     }
     ARK_CUDA_TRY(cudaGraphInstantiate(&s->gexec[slot], g, 0));
-    const void* key[4] = {w16, g16, m, v};
+    const void* key[5] = {w16, g16, m, v, w32};
     memcpy(s->gkey[slot], key, sizeof(key));
     return ARK_OK;
 }
@@ -940,6 +954,11 @@ int ark_cuda_opt_init(const ark_opt_cfg* cfg, ark_opt_state** out) {
     if (const char* e = getenv("ARK_PASS2_VARIANT")) var2 = atoi(e);
     if (var2 < 0 || var2 >= (int)(sizeof(kPass2Variants) / sizeof(kPass2Variants[0]))) var2 = 0;
     s->pass2 = kPass2Variants[var2].fn;
+    // with the FP32 weight copy the 2-group shape needs 146 registers (1 block
+    // per SM), so that mode always uses 1 group x 3 blocks/SM
+    s->pass2_w32 = kPass2Variants[1].fn_w32;
+    s->blocks2w = streaming_grid(reinterpret_cast<const void*>(s->pass2_w32), kThreads, 0,
+                                 (cfg->n >> 3) / kPass2Variants[1].unroll + 1);
     s->blocks1r = streaming_grid(reinterpret_cast<const void*>(kPass1Reduce), kThreads, 0,
                                  (cfg->n >> 3) / 2 + 1);
     s->blocks2 = streaming_grid(reinterpret_cast<const void*>(s->pass2), kThreads, 0,
@@ -1008,10 +1027,10 @@ int ark_cuda_opt_init(const ark_opt_cfg* cfg, ark_opt_state** out) {
 }
 
 static int run_step(ark_opt_state* s, uint16_t* w16, const uint16_t* g16, float* m, float* v,
-                    bool reduce) {
+                    float* w32, bool reduce) {
     if (!s) return ARK_E_INVALID_ARG;
     if (s->cfg.n && (!w16 || !g16 || !m || !v)) return ARK_E_INVALID_ARG;
-    if (!aligned16(w16) || !aligned16(g16) || !aligned16(m) || !aligned16(v))
+    if (!aligned16(w16) || !aligned16(g16) || !aligned16(m) || !aligned16(v) || !aligned16(w32))
         return ARK_E_MISALIGNED;
     if (reduce) {
         if (!s->gbuf) return ARK_E_INVALID_ARG;          // no ark_cuda_opt_grad_buffer yet
@@ -1022,14 +1041,14 @@ static int run_step(ark_opt_state* s, uint16_t* w16, const uint16_t* g16, float*
     const bool profile = s->prof_used < s->prof_cap;
     cudaEvent_t* ev = profile ? &s->prof_events[4 * s->prof_used] : nullptr;
     if (!(s->cfg.flags & ARK_OPT_USE_GRAPH)) {
-        const int rc = enqueue_step(s, s->stream, w16, g16, m, v, ev, false, reduce);
+        const int rc = enqueue_step(s, s->stream, w16, g16, m, v, w32, ev, false, reduce);
         if (rc == ARK_OK && profile) s->prof_used++;
         return rc;
     }
     const int slot = (reduce ? 2 : 0) + (profile ? 1 : 0);
-    const void* key[4] = {w16, g16, m, v};
+    const void* key[5] = {w16, g16, m, v, w32};
     if (!s->gexec[slot] || memcmp(key, s->gkey[slot], sizeof(key)) != 0) {
-        const int rc = capture_graph(s, slot, w16, g16, m, v);
+        const int rc = capture_graph(s, slot, w16, g16, m, v, w32);
         if (rc != ARK_OK) {
             drop_graph(s, slot);
             return rc;
@@ -1045,12 +1064,18 @@ static int run_step(ark_opt_state* s, uint16_t* w16, const uint16_t* g16, float*
 }
 
 int ark_cuda_opt_step(ark_opt_state* s, uint16_t* w16, const uint16_t* g16, float* m, float* v) {
-    return run_step(s, w16, g16, m, v, false);
+    return run_step(s, w16, g16, m, v, nullptr, false);
 }
 
 int ark_cuda_opt_step_reduce(ark_opt_state* s, uint16_t* w16, uint16_t* g16_shard, float* m,
                              float* v) {
-    return run_step(s, w16, g16_shard, m, v, true);
+    return run_step(s, w16, g16_shard, m, v, nullptr, true);
+}
+
+int ark_cuda_opt_step_ex(ark_opt_state* s, uint16_t* w16, uint16_t* g16, float* m, float* v,
+                         float* w32_out, uint32_t options) {
+    if (options & ~ARK_STEP_REDUCE) return ARK_E_INVALID_ARG;
+    return run_step(s, w16, g16, m, v, w32_out, (options & ARK_STEP_REDUCE) != 0);
 }
 
 int ark_cuda_opt_grad_buffer(ark_opt_state* s, uint64_t n_full, uint16_t** out) {

@@ -199,6 +199,16 @@ class Optimizer:
             _ptr(m, "f32", self.n), _ptr(v, "f32", self.n))
         _lib.check("ark_cuda_opt_step_reduce", rc)
 
+    def step_all_w32(self, w16, g16, m, v, w32, reduce: bool = False):
+        """step_all (or step_reduce) that also writes the updated weights
+        widened to FP32 into w32 -- the forward's copy, in place of a
+        separate dequant of every weight tensor each step."""
+        rc = _lib.lib().ark_cuda_opt_step_ex(
+            self._h, _ptr(w16, "f16", self.n), _ptr(g16, "f16", self.n), _ptr(m, "f32", self.n),
+            _ptr(v, "f32", self.n), _ptr(w32, "f32", self.n),
+            _lib.ARK_STEP_REDUCE if reduce else 0)
+        _lib.check("ark_cuda_opt_step_ex", rc)
+
     def upload_grads(self, g16_dev, g16_host):
         """Asynchronous H2D copy of this shard's scaled grads (host tensor or
         numpy array; pinned memory for full speed)."""

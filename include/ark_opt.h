@@ -224,6 +224,20 @@ ARK_API int ark_cuda_opt_grad_buffer(ark_opt_state* st, uint64_t n_full, uint16_
 ARK_API int ark_cuda_opt_step_reduce(ark_opt_state* st, uint16_t* w16, uint16_t* g16_shard,
                                      float* m, float* v);
 
+/* ark_cuda_opt_step / ark_cuda_opt_step_reduce with options:
+ *  - options & ARK_STEP_REDUCE: the reduce-scatter step (g16 receives the
+ *    reduced shard), else g16 holds this rank's scaled FP16 grads;
+ *  - w32_out (NULL: none; else cfg.n FP32, 16-byte aligned): every step
+ *    that updates the weights also writes them widened to FP32, the copy
+ *    the forward reads -- replacing the per-step ark_dequant_f16_to_f32 of
+ *    every weight tensor (src/training.rs:165-186) by 4 extra bytes per
+ *    parameter in pass 2.  A skipped step leaves w16 and w32_out as they
+ *    are, so w32_out must be initialised once (dequant) before the first
+ *    step. */
+#define ARK_STEP_REDUCE 0x1u
+ARK_API int ark_cuda_opt_step_ex(ark_opt_state* st, uint16_t* w16, uint16_t* g16, float* m,
+                                 float* v, float* w32_out, uint32_t options);
+
 /* Wait for the state's stream and copy the device state out.  Returns
  * ARK_E_EARLY_STOP once the early-stop condition holds (training.rs:298),
  * a device error code if one was raised, else ARK_OK. */

@@ -10,6 +10,7 @@ import numpy as np
 import pytest
 import torch
 import torch.multiprocessing as mp
+from gpu_util import same_f16
 
 pytestmark = pytest.mark.gpu
 
@@ -268,7 +269,8 @@ def test_reduce_scatter_step_matches_oracle(oracle, world):
         ref_states.append((st.loss_scale, st.opt_step, st.last_overflow, st.clean_steps))
     for rank, lo, hi, ws, ms, vs, sts, shards in res:
         for k in range(4):
-            assert np.array_equal(shards[k], ref_shards[k][lo:hi]), (rank, k)
+            # NaN payloads differ (CUDA returns a canonical NaN); any NaN matches
+            assert same_f16(shards[k], ref_shards[k][lo:hi]), (rank, k)
             s = sts[k]
             assert (s["loss_scale"], s["opt_step"], s["last_overflow"], s["clean_steps"]) == \
                 ref_states[k], (rank, k)

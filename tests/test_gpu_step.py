@@ -234,9 +234,48 @@ def test_reduce_step_single_rank(oracle, shard):
             g_full[lo + 5] = 0x7C00
         opt.step_reduce(dw, shard_g, dm, dv)
         g = oracle.reduce_f16([g_full], n, lo)
-        assert np.array_equal(host(shard_g), g)
+        assert same_f16(host(shard_g), g)
         s, bad = oracle.partial_f16(cfg, ost, g, lo)
         oracle.apply_f16(cfg, ost, w, g, m, v, lo, s, bad)
         check_state(opt.status(), ost, f"step {k}")
+    assert same_f16(host(dw), w) and same_f32(host(dm), m) and same_f32(host(dv), v)
+    opt.close()
+
+
+@pytest.mark.parametrize("reduce", [False, True])
+def test_step_writes_fp32_weight_copy(oracle, reduce):
+    """ark_cuda_opt_step_ex with w32_out: the updated weights widened to FP32
+    (the forward's copy, training.rs:165-186) on every updating step; a
+    skipped step leaves them alone."""
+    L = tiny()
+    opt = ab.Optimizer(L, ab.AdamConfig(lr=3e-4, beta1=0.9, beta2=0.95, eps=1e-8,
+                                        weight_decay=0.1, grad_clip=1.0),
+                       ab.LossScaleConfig(init=65536.0, every=50, max=2.0 ** 24),
+                       constant_lr=True, initial_step=999)
+    n = opt.n
+    w, g, m, v = oracle_bufs(oracle, n, 0, SEED, 65536.0)
+    dw, dg, dm, dv = dev(w), dev(g), dev(m), dev(v)
+    if reduce:
+        full = opt.grad_buffer()
+        full.copy_(dg)
+    w32 = torch.from_numpy(oracle.dequant(w)).cuda()
+    cfg = oracle.make_cfg(n_decay=L.n_decay, scale_every=50, scale_max=2.0 ** 24)
+    ost = oracle.make_state(65536.0, opt_step=999)
+    for k in range(1, 4):
+        if k == 2:
+            g[7] = 0x7C00
+            (full if reduce else dg).view(torch.int16)[7] = 0x7C00
+        if k == 3:
+            g[7] = oracle.synth_f16(1, 7, SEED, synth.STREAM_G, 1e-3, 65536.0)[0]
+            (full if reduce else dg).view(torch.int16)[7] = int(np.int16(np.uint16(g[7]).view(np.int16)))
+        before = host(w32).copy()
+        opt.step_all_w32(dw, dg, dm, dv, w32, reduce=reduce)
+        s, bad = oracle.partial_f16(cfg, ost, g, 0)
+        oracle.apply_f16(cfg, ost, w, g, m, v, 0, s, bad)
+        check_state(opt.status(), ost, f"step {k}")
+        if k == 2:
+            assert np.array_equal(host(w32).view(np.uint32), before.view(np.uint32))
+        else:
+            assert same_f32(host(w32), oracle.dequant(w))
     assert same_f16(host(dw), w) and same_f32(host(dm), m) and same_f32(host(dv), v)
     opt.close()
