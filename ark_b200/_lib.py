@@ -26,6 +26,7 @@ ARK_OPT_COMPAT_GAMMA_FINAL_UNSCALED = 0x1
 ARK_OPT_USE_GRAPH = 0x2
 ARK_OPT_NCCL_EXCHANGE = 0x4
 ARK_STEP_REDUCE = 0x1
+ARK_CKPT_RESTORE_SCALE = 0x1
 
 c_f, c_u32, c_u64, c_i, c_i32, c_d, c_p = (ctypes.c_float, ctypes.c_uint32, ctypes.c_uint64,
                                            ctypes.c_int, ctypes.c_int32, ctypes.c_double,
@@ -44,6 +45,11 @@ class OptCfg(ctypes.Structure):
         ("initial_step", c_u32), ("flags", c_u32), ("rank", c_i32), ("world_size", c_i32),
         ("nccl_comm", c_p), ("stream", c_p), ("wait_timeout_ms", c_u32), ("reserved", c_u32),
     ]
+
+
+class CkptTensor(ctypes.Structure):
+    """ark_ckpt_tensor."""
+    _fields_ = [("numel", c_u64), ("flat_offset", c_u64)]
 
 
 class OptStatus(ctypes.Structure):
@@ -89,6 +95,10 @@ SIGNATURES = {
                                     ctypes.POINTER(c_u32)]),
     "ark_cuda_opt_destroy": (c_i, [c_p]),
     "ark_cuda_lr_schedule": (c_i, [ctypes.POINTER(c_f), c_u32, c_f, c_u32]),
+    "ark_cuda_ckpt_save": (c_i, [c_p, ctypes.c_char_p, ctypes.POINTER(CkptTensor), c_u32, c_u64,
+                                 c_p, c_p, c_p]),
+    "ark_cuda_ckpt_load": (c_i, [c_p, ctypes.c_char_p, ctypes.POINTER(CkptTensor), c_u32,
+                                 ctypes.POINTER(c_u64), c_p, c_p, c_p, c_u32]),
     "ark_cuda_nccl_unique_id": (c_i, [c_p]),
     "ark_cuda_nccl_comm_init": (c_i, [c_i, c_i, c_p, c_i, ctypes.POINTER(c_p)]),
     "ark_cuda_nccl_comm_destroy": (c_i, [c_p]),

@@ -36,4 +36,12 @@ __host__ __device__ inline bool aligned16(const void* p) {
 // with as many resident blocks as the kernel's occupancy allows.
 int streaming_grid(const void* kernel, int threads, size_t dyn_smem, uint64_t work_items);
 
+// What the checkpoint code needs of an optimizer state (ark_step.cu).
+struct OptView {
+    int device, rank, world;
+    uint64_t n, shard_offset;
+    float scale_init;
+};
+int opt_view(const ark_opt_state* st, OptView* out);
+
 }  // namespace ark

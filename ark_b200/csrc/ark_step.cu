@@ -1194,6 +1194,21 @@ int ark_cuda_opt_profile_read(ark_opt_state* s, float* out, uint32_t capacity, u
     return ARK_OK;
 }
 
+}  // extern "C"
+
+int ark::opt_view(const ark_opt_state* s, OptView* out) {
+    if (!s || !out) return ARK_E_INVALID_ARG;
+    out->device = s->device;
+    out->rank = s->cfg.rank;
+    out->world = s->cfg.world_size;
+    out->n = s->cfg.n;
+    out->shard_offset = s->cfg.shard_offset;
+    out->scale_init = s->cfg.scale_init;
+    return ARK_OK;
+}
+
+extern "C" {
+
 int ark_cuda_opt_geometry(ark_opt_state* s, uint32_t* b1, uint32_t* b2, uint32_t* threads) {
     if (!s) return ARK_E_INVALID_ARG;
     if (b1) *b1 = (uint32_t)s->blocks1;

@@ -271,6 +271,39 @@ ARK_API int ark_cuda_opt_geometry(ark_opt_state* st, uint32_t* pass1_blocks, uin
 
 ARK_API int ark_cuda_opt_destroy(ark_opt_state* st);
 
+/* ---- ARK4 checkpoints from device shards (src/io.rs:12-24, 410-671;
+ *      rotation and call site src/training.rs:536-604) ------------------
+ * tensors: the model tensors in ARK4 file order -- embed, then per layer
+ * wq wk wv wo w1 w2 w3 g1 g2, then gamma_final (2 + 9 L entries) -- each
+ * with its element count and its offset in the flat index space of the
+ * optimizer state.  Every rank calls with its own shard (w16 / m / v, cfg.n
+ * elements) and writes or reads only that shard's bytes of the one file;
+ * rank 0 also writes the header and a trailer with the loss-scale state
+ * (ignored by the reference's reader).  A reader must not start before
+ * every writer has returned. */
+typedef struct ark_ckpt_tensor {
+    uint64_t numel;
+    uint64_t flat_offset;
+} ark_ckpt_tensor;
+
+/* adam_step is the device optimizer step (optimizer.rs:70). */
+ARK_API int ark_cuda_ckpt_save(ark_opt_state* st, const char* path,
+                               const ark_ckpt_tensor* tensors, uint32_t n_tensors,
+                               uint64_t global_step, const uint16_t* w16, const float* m,
+                               const float* v);
+
+/* Reads ARK4 (and ARK3: FP32 weights rounded to FP16, memory.rs:347-377)
+ * into this rank's shard and sets the device step to the file's adam_step
+ * (optimizer.rs:308).  The loss-scale state is restored from the trailer
+ * with ARK_CKPT_RESTORE_SCALE, else reset to cfg.scale_init as the reference
+ * does on resume (training.rs:120).  Record headers that do not match the
+ * layout are an error (ARK_E_INVALID_ARG), not a silent cold start. */
+#define ARK_CKPT_RESTORE_SCALE 0x1u
+ARK_API int ark_cuda_ckpt_load(ark_opt_state* st, const char* path,
+                               const ark_ckpt_tensor* tensors, uint32_t n_tensors,
+                               uint64_t* global_step, uint16_t* w16, float* m, float* v,
+                               uint32_t flags);
+
 /* Build the reference lr schedule (optimizer.rs:80-92: linear warmup, then
  * cosine to lr/10 over 800k steps, all in f32) into a host table of
  * len entries, entry t = lr for optimizer step t. */
