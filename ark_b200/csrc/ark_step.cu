@@ -308,8 +308,10 @@ __global__ void __launch_bounds__(kThreads, MINB) pass1_kernel(StepParams p) {
 // complete (gradients-ready epoch in every peer's slot) and waits, bounded,
 // for every peer's announcement; the partial exchange at the end of pass 1
 // then proves that every peer has finished reading this rank's buffer.
-template <int U, int MINB>
-__global__ void __launch_bounds__(kThreads, MINB) pass1_reduce_kernel(StepParams p) {
+// Gradients-ready barrier of the reduce-scatter step: block 0 publishes
+// this rank's epoch into every peer's slot; every block waits (bounded) for
+// every peer's.  Returns true (in all threads) if a peer never showed up.
+__device__ bool reduce_ready_barrier(const StepParams& p) {
     __shared__ int s_fail;
     const unsigned long long epoch = p.st->steps_called + 1ull;
     if (threadIdx.x == 0) s_fail = 0;
@@ -333,7 +335,12 @@ __global__ void __launch_bounds__(kThreads, MINB) pass1_reduce_kernel(StepParams
         }
     }
     __syncthreads();
-    const bool failed = s_fail != 0;
+    return s_fail != 0;
+}
+
+template <int U, int MINB>
+__global__ void __launch_bounds__(kThreads, MINB) pass1_reduce_kernel(StepParams p) {
+    const bool failed = reduce_ready_barrier(p);
     const P1Scale sc = p1_scale(p);
     P1Acc a;
     const uint64_t nvec = p.n >> 3;
@@ -572,6 +579,64 @@ __global__ void __launch_bounds__(kThreads, MINB) pass2_kernel(StepParams p,
     if (threadIdx.x == 0) advance_state(p, pl);
 }
 
+// The same for a fixed rank count NR: all NR x U loads of a thread are in
+// flight before any addition (remote loads over NVLink have long latency).
+template <int NR, int U, int MINB>
+__global__ void __launch_bounds__(kThreads, MINB) pass1_reduce_nr_kernel(StepParams p) {
+    const bool failed = reduce_ready_barrier(p);
+    const P1Scale sc = p1_scale(p);
+    P1Acc a;
+    const uint64_t nvec = p.n >> 3;
+    const uint64_t stride = (uint64_t)gridDim.x * kThreads;
+    uint4* out = reinterpret_cast<uint4*>(p.g16_out);
+    const uint4* src[NR];
+#pragma unroll
+    for (int r = 0; r < NR; ++r) src[r] = reinterpret_cast<const uint4*>(p.gsrc[r] + p.offset);
+    if (!failed) {
+        for (uint64_t base = (uint64_t)blockIdx.x * kThreads + threadIdx.x; base < nvec;
+             base += stride * U) {
+            uint4 q[NR][U];
+#pragma unroll
+            for (int r = 0; r < NR; ++r)
+#pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    const uint64_t i = base + u * stride;
+                    q[r][u] = i < nvec ? __ldcg(src[r] + i) : make_uint4(0, 0, 0, 0);
+                }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const uint64_t i = base + u * stride;
+                if (i >= nvec) continue;
+                float acc[8];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
+#pragma unroll
+                for (int r = 0; r < NR; ++r) {                 // rank order
+                    const uint32_t w[4] = {q[r][u].x, q[r][u].y, q[r][u].z, q[r][u].w};
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        acc[j] = __fadd_rn(acc[j], h2f((j & 1) ? hi16(w[j >> 1]) : lo16(w[j >> 1])));
+                }
+                uint32_t w[4];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) w[k] = pack16(f2h(acc[2 * k]), f2h(acc[2 * k + 1]));
+                const uint4 rq = make_uint4(w[0], w[1], w[2], w[3]);
+                out[i] = rq;
+                p1_consume(a, rq, i, sc, p);
+            }
+        }
+        if (blockIdx.x == 0 && threadIdx.x < (p.n & 7u)) {   // ragged tail (n % 8)
+            const uint64_t i = (nvec << 3) + threadIdx.x;
+            float f = 0.0f;
+            for (int r = 0; r < NR; ++r) f = __fadd_rn(f, h2f(p.gsrc[r][p.offset + i]));
+            const uint16_t h = f2h(f);
+            p.g16_out[i] = h;
+            p1_consume1(a, h, i, sc, p);
+        }
+    }
+    p1_finish(a, sc, failed, p);
+}
+
 // launch-shape variants: vectors in flight per thread x minimum resident blocks
 using Pass1Fn = void (*)(StepParams);
 using Pass2Fn = void (*)(StepParams, uint16_t*, float*, float*);
@@ -590,7 +655,16 @@ static const Pass1Variant kPass1Variants[] = {
     {8, 4, pass1_kernel<8, 4>},
     {16, 2, pass1_kernel<16, 2>},
 };
-static const Pass1Fn kPass1Reduce = pass1_reduce_kernel<2, 4>;
+// reduce-scatter pass 1 by rank count (any other count: the generic kernel)
+static Pass1Fn pass1_reduce_for(int world) {
+    switch (world) {
+        case 1: return pass1_reduce_nr_kernel<1, 8, 4>;
+        case 2: return pass1_reduce_nr_kernel<2, 4, 4>;
+        case 4: return pass1_reduce_nr_kernel<4, 2, 4>;
+        case 8: return pass1_reduce_nr_kernel<8, 1, 4>;
+        default: return pass1_reduce_kernel<2, 4>;
+    }
+}
 static const Pass2Variant kPass2Variants[] = {
     {2, 1, pass2_kernel<2, 1, false>, pass2_kernel<2, 1, true>},
     {1, 3, pass2_kernel<1, 3, false>, pass2_kernel<1, 3, true>},
@@ -621,7 +695,7 @@ struct ark_opt_state {
     Partial* d_part_all = nullptr;
     ark_opt_status* h_status = nullptr;  // pinned
     int blocks1 = 0, blocks2 = 0, blocks1r = 0;
-    Pass1Fn pass1 = nullptr;                  // chosen launch-shape variants
+    Pass1Fn pass1 = nullptr, pass1r = nullptr;   // chosen launch-shape variants
     Pass2Fn pass2 = nullptr, pass2_w32 = nullptr;
     int blocks2w = 0;
     // P2P exchange slots (world > 1)
@@ -834,7 +908,7 @@ int enqueue_step(ark_opt_state* s, cudaStream_t stream, uint16_t* w16, const uin
     if (reduce) p.g16_out = const_cast<uint16_t*>(g16);
     p.w32_out = w32;
     if (ev) ARK_RECORD(ev[0], stream);
-    if (reduce) kPass1Reduce<<<s->blocks1r, kThreads, 0, stream>>>(p);
+    if (reduce) s->pass1r<<<s->blocks1r, kThreads, 0, stream>>>(p);
     else s->pass1<<<s->blocks1, kThreads, 0, stream>>>(p);
     ARK_CUDA_TRY(cudaGetLastError());
     if (ev) ARK_RECORD(ev[1], stream);
@@ -959,8 +1033,9 @@ int ark_cuda_opt_init(const ark_opt_cfg* cfg, ark_opt_state** out) {
     s->pass2_w32 = kPass2Variants[1].fn_w32;
     s->blocks2w = streaming_grid(reinterpret_cast<const void*>(s->pass2_w32), kThreads, 0,
                                  (cfg->n >> 3) / kPass2Variants[1].unroll + 1);
-    s->blocks1r = streaming_grid(reinterpret_cast<const void*>(kPass1Reduce), kThreads, 0,
-                                 (cfg->n >> 3) / 2 + 1);
+    s->pass1r = pass1_reduce_for(cfg->world_size);
+    s->blocks1r = streaming_grid(reinterpret_cast<const void*>(s->pass1r), kThreads, 0,
+                                 (cfg->n >> 3) + 1);
     s->blocks2 = streaming_grid(reinterpret_cast<const void*>(s->pass2), kThreads, 0,
                                 (cfg->n >> 3) / kPass2Variants[var2].unroll + 1);
     const int W = cfg->world_size;

@@ -264,6 +264,69 @@ def cpu_baseline_single_thread(L, budget_s=20.0):
                       f"{t * 1e3:.0f} ms/step"}
 
 
+def measure_aux(opt, L, w16, g16, m, v, stream, args, max_over_ranks, barrier):
+    """Rows next to the path, timed with CUDA events on the step's stream:
+    the step that also writes the forward's FP32 weights vs the step plus
+    the reference's separate per-step dequant (legacy ark_dequant_f16_to_f32),
+    and ARK4 checkpoint save / load of this rank's shard."""
+    import torch
+
+    import ark_b200 as ab
+    from ark_b200 import checkpoint
+    n = opt.n
+    k = max(3, min(args.steps, 200))
+    w32 = torch.empty(n, dtype=torch.float32, device=w16.device)
+    ab.dequant_f16_to_f32(w16, w32)
+
+    def timed(fn):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier()
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(k):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier()
+        return max_over_ranks(e0.elapsed_time(e1) / k)
+
+    t_w32 = timed(lambda: opt.step_all_w32(w16, g16, m, v, w32))
+
+    def step_then_dequant():
+        opt.step_all(w16, g16, m, v)
+        ab.dequant_f16_to_f32(w16, w32)     # legacy entry point: synchronous per call
+
+    ab.legacy_set_async(True)
+    t_sep = timed(step_then_dequant)
+    ab.legacy_set_async(False)
+    out = {"step_with_fp32_weights_ms": round(t_w32, 4),
+           "step_then_dequant_ms": round(t_sep, 4),
+           "fp32_copy_saving_ms": round(t_sep - t_w32, 4)}
+    if args.ckpt_dir and L.tensors[0].name == "embed":
+        import time
+        path = os.path.join(args.ckpt_dir, f"ark_bench_{os.getpid() if opt.world == 1 else 'x'}.bin")
+        if opt.world > 1:
+            path = os.path.join(args.ckpt_dir, "ark_bench_sharded.bin")
+        barrier()
+        t0 = time.perf_counter()
+        checkpoint.save(opt, path, w16, m, v, global_step=1)
+        barrier()
+        t_save = max_over_ranks(time.perf_counter() - t0)
+        t0 = time.perf_counter()
+        checkpoint.load(opt, path, w16, m, v)
+        barrier()
+        t_load = max_over_ranks(time.perf_counter() - t0)
+        size = os.path.getsize(path)
+        out["checkpoint"] = {"file_bytes": size, "save_s": round(t_save, 3),
+                             "load_s": round(t_load, 3),
+                             "save_gbs": round(size / t_save / 1e9, 2),
+                             "load_gbs": round(size / t_load / 1e9, 2), "path": args.ckpt_dir}
+        barrier()
+        if opt.rank == 0:
+            os.unlink(path)
+    return out
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -393,6 +456,9 @@ def run_ours(args):
     clk = clocks.summary()
     geom = opt.geometry()
 
+    aux = measure_aux(opt, L, w16, g16, m, v, stream, args, max_over_ranks, barrier) \
+        if args.aux else None
+
     cpu = None
     if (rank == 0 and world == 1 and not args.no_cpu_baseline and not args.params
             and args.workload == "eko"):
@@ -427,6 +493,7 @@ def run_ours(args):
                     "path": "Optimizer.upload_grads (pinned host fp16 grads) + step_all + "
                             "status() per step, through the C ABI"},
             "gpu_launches": 2 * args.steps,
+            "aux": aux,
             "clocks": clk,
         }
         print(json.dumps(line), flush=True)
@@ -444,6 +511,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--params", type=int, default=0,
                     help="flat-buffer workload of this many params instead of EKO-237M")
+    ap.add_argument("--aux", action="store_true",
+                    help="also time the FP32-weight-copy step and ARK4 checkpoint save/load")
+    ap.add_argument("--ckpt-dir", default="",
+                    help="directory for the --aux checkpoint files (default: none)")
     ap.add_argument("--reduce", action="store_true",
                     help="include the gradient hand-off: reduce-scatter of every rank's full "
                          "FP16 gradients over NVLink, fused with pass 1")
