@@ -670,6 +670,7 @@ static const Pass2Variant kPass2Variants[] = {
     {1, 3, pass2_kernel<1, 3, false>, pass2_kernel<1, 3, true>},
     {1, 4, pass2_kernel<1, 4, false>, pass2_kernel<1, 4, true>},
     {3, 1, pass2_kernel<3, 1, false>, pass2_kernel<3, 1, true>},
+    {2, 2, pass2_kernel<2, 2, false>, pass2_kernel<2, 2, true>},
 };
 
 }  // namespace ark
@@ -1022,17 +1023,21 @@ int ark_cuda_opt_init(const ark_opt_cfg* cfg, ark_opt_state** out) {
     s->pass1 = kPass1Variants[var].fn;
     s->blocks1 = streaming_grid(reinterpret_cast<const void*>(s->pass1), kThreads, 0,
                                 (cfg->n >> 3) / kPass1Variants[var].unroll + 1);
-    // pass 2: 2 groups in flight x 2 blocks/SM for large shards, 1 group x 3
-    // blocks/SM below 100M params (shorter tail; EKO/4 and EKO/8 sweep)
-    int var2 = cfg->n < 100000000ull ? 1 : 0;
+    // pass 2: 2 groups in flight x 2 blocks/SM (<= 128 registers) for large
+    // shards, 1 group x 3 blocks/SM below 100M params (shorter tail); from the
+    // B200 sweeps at the EKO, EKO/4 and EKO/8 shard sizes
+    int var2 = cfg->n < 100000000ull ? 1 : 4;
     if (const char* e = getenv("ARK_PASS2_VARIANT")) var2 = atoi(e);
     if (var2 < 0 || var2 >= (int)(sizeof(kPass2Variants) / sizeof(kPass2Variants[0]))) var2 = 0;
     s->pass2 = kPass2Variants[var2].fn;
-    // with the FP32 weight copy the 2-group shape needs 146 registers (1 block
-    // per SM), so that mode always uses 1 group x 3 blocks/SM
-    s->pass2_w32 = kPass2Variants[1].fn_w32;
+    // with the FP32 weight copy: 2 groups x 2 blocks/SM (122 registers) is
+    // the fastest shape on B200 (EKO: 1.161 ms vs 1.237 ms for 1 x 3)
+    int varw = 4;
+    if (const char* e = getenv("ARK_PASS2W_VARIANT")) varw = atoi(e);
+    if (varw < 0 || varw >= (int)(sizeof(kPass2Variants) / sizeof(kPass2Variants[0]))) varw = 4;
+    s->pass2_w32 = kPass2Variants[varw].fn_w32;
     s->blocks2w = streaming_grid(reinterpret_cast<const void*>(s->pass2_w32), kThreads, 0,
-                                 (cfg->n >> 3) / kPass2Variants[1].unroll + 1);
+                                 (cfg->n >> 3) / kPass2Variants[varw].unroll + 1);
     s->pass1r = pass1_reduce_for(cfg->world_size);
     s->blocks1r = streaming_grid(reinterpret_cast<const void*>(s->pass1r), kThreads, 0,
                                  (cfg->n >> 3) + 1);
