@@ -85,3 +85,19 @@ def test_missing_library_fails_loudly(monkeypatch):
     monkeypatch.setattr(_lib, "_LIB", None)
     with pytest.raises(RuntimeError, match="no CPU fallback"):
         _lib.lib()
+
+
+def build_c_example(tmp_path):
+    exe = tmp_path / "step_from_c"
+    src = os.path.join(ROOT, "ark_b200", "examples", "step_from_c.c")
+    libdir = os.path.dirname(_lib.LIB_PATH)
+    subprocess.run(["gcc", "-std=c11", "-Wall", "-Werror", "-I", os.path.join(ROOT, "include"),
+                    "-I", "/usr/local/cuda/include", src, "-L", libdir, "-lark_cuda",
+                    "-L", "/usr/local/cuda/lib64", "-lcudart", f"-Wl,-rpath,{libdir}",
+                    "-Wl,-rpath,/usr/local/cuda/lib64", "-o", str(exe)], check=True)
+    return exe
+
+
+def test_plain_c_caller_compiles_and_links(tmp_path):
+    """The header is plain C and the library links from a C program."""
+    assert build_c_example(tmp_path).exists()
