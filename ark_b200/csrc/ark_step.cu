@@ -110,13 +110,18 @@ __device__ __forceinline__ void accum8_general(uint4 q, uint64_t gi0, float inv,
 // Power-of-two loss scale (the only kind the state machine produces from a
 // power-of-two init, backoff and growth): fp32(h) * inv is exact, so the sum
 // of squared unscaled gradients is inv^2 * sum(h^2), with h^2 exact in
-// double.  Elements in the kept range (compat mode) go to acc_k unscaled.
-// Two accumulators halve the dependent chain of double FMAs.
+// double.  With KEEP, elements in the kept range (compat mode) go to acc_k
+// unscaled; without it the range is empty and no index is compared.  Two
+// accumulators halve the dependent chain of double FMAs.  An inf or NaN
+// gradient makes its square, and from then on the accumulator, non-finite;
+// a finite h^2 is at most 2^32, so a finite sum never overflows: the
+// accumulators double as the non-finite check.
+template <bool KEEP>
 __device__ __forceinline__ void accum8_pow2(uint4 q, uint64_t gi0, uint64_t keep_lo,
                                             uint64_t keep_hi, double& acc0, double& acc1,
                                             double& acc_k) {
     const uint32_t w[4] = {q.x, q.y, q.z, q.w};
-    if (gi0 + 8 > keep_lo && gi0 < keep_hi) {           // rare: straddles the kept range
+    if (KEEP && gi0 + 8 > keep_lo && gi0 < keep_hi) {   // rare: straddles the kept range
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
             const double d = h2d((j & 1) ? hi16(w[j >> 1]) : lo16(w[j >> 1]));
@@ -187,24 +192,42 @@ struct P1Scale {
     bool pow2;
 };
 
+// pow2: inv is a power of two for which fp32(h) * inv is exact for every
+// finite FP16 h (2^-102 <= inv <= 2^111: no f32 underflow or overflow);
+// any other scale takes the general path, which rounds like the reference.
 __device__ __forceinline__ P1Scale p1_scale(const StepParams& p) {
     P1Scale sc;
     sc.inv = __fdiv_rn(1.0f, p.st->loss_scale);   // training.rs:244
     const uint32_t ib = __float_as_uint(sc.inv);
-    sc.pow2 = (ib & 0x7FFFFFu) == 0 && (ib & 0x7F800000u) != 0 &&
-              (ib & 0x7F800000u) != 0x7F800000u;
+    const uint32_t e = (ib >> 23) & 0xFFu;
+    sc.pow2 = (ib & 0x807FFFFFu) == 0 && e >= 127u - 102u && e <= 127u + 111u;
     return sc;
 }
 
+// One 8-element vector.  POW2 takes its non-finite check from the
+// accumulators (accum8_pow2); the general path, where fp32(h) * inv may
+// overflow for a finite h, checks the FP16 bit patterns.
+template <bool KEEP, bool POW2>
 __device__ __forceinline__ void p1_consume(P1Acc& a, const uint4 q, uint64_t vec,
                                            const P1Scale& sc, const StepParams& p) {
-    a.amax = absmax2(a.amax, q.x);
-    a.amax = absmax2(a.amax, q.y);
-    a.amax = absmax2(a.amax, q.z);
-    a.amax = absmax2(a.amax, q.w);
     const uint64_t gi0 = p.offset + (vec << 3);
-    if (sc.pow2) accum8_pow2(q, gi0, p.keep_lo, p.keep_hi, a.acc0, a.acc1, a.acc_k);
-    else accum8_general(q, gi0, sc.inv, p.keep_lo, p.keep_hi, a.acc0, a.acc1);
+    if (POW2) {
+        accum8_pow2<KEEP>(q, gi0, p.keep_lo, p.keep_hi, a.acc0, a.acc1, a.acc_k);
+    } else {
+        a.amax = absmax2(a.amax, q.x);
+        a.amax = absmax2(a.amax, q.y);
+        a.amax = absmax2(a.amax, q.z);
+        a.amax = absmax2(a.amax, q.w);
+        accum8_general(q, gi0, sc.inv, p.keep_lo, p.keep_hi, a.acc0, a.acc1);
+    }
+}
+
+// Either path, chosen per step by the loss scale (uniform across the grid).
+template <bool KEEP>
+__device__ __forceinline__ void p1_consume_any(P1Acc& a, const uint4 q, uint64_t vec,
+                                               const P1Scale& sc, const StepParams& p) {
+    if (sc.pow2) p1_consume<KEEP, true>(a, q, vec, sc, p);
+    else p1_consume<KEEP, false>(a, q, vec, sc, p);
 }
 
 __device__ __forceinline__ void p1_consume1(P1Acc& a, uint16_t h, uint64_t i, const P1Scale& sc,
@@ -233,8 +256,9 @@ __device__ void p1_finish(const P1Acc& a, const P1Scale& sc, bool failed, const 
     const double inv_d = (double)sc.inv;
     const double acc_s = a.acc0 + a.acc1;
     const double acc = sc.pow2 ? __fma_rn(acc_s, inv_d * inv_d, a.acc_k) : acc_s;
+    const bool raw_nonfinite = sc.pow2 && !isfinite(acc_s + a.acc_k);
     const unsigned long long bad =
-        ((a.amax & 0xFFFFu) >= 0x7C00u) || ((a.amax >> 16) >= 0x7C00u);
+        raw_nonfinite || ((a.amax & 0xFFFFu) >= 0x7C00u) || ((a.amax >> 16) >= 0x7C00u);
     const double bsum = block_sum<kThreads>(acc, s_sum);
     const unsigned long long bbad = block_sum_u64<kThreads>(bad, s_bad);
     const unsigned long long bfail = block_sum_u64<kThreads>(failed ? 1ull : 0ull, s_bad);
@@ -269,29 +293,44 @@ __device__ void p1_finish(const P1Acc& a, const P1Scale& sc, bool failed, const 
     }
 }
 
-template <int U, int MINB>
-__global__ void __launch_bounds__(kThreads, MINB) pass1_kernel(StepParams p) {
-    const P1Scale sc = p1_scale(p);
-    P1Acc a;
+// The grid-stride stream of pass 1: rounds of U vectors per thread, loads
+// issued before any is consumed; rounds entirely in range run without
+// per-vector bounds checks, and the one partial round after them with.
+template <int U, bool KEEP, bool POW2>
+__device__ __forceinline__ void p1_stream(P1Acc& a, const P1Scale& sc, const StepParams& p) {
     const uint4* g = reinterpret_cast<const uint4*>(p.g16);
     const uint64_t nvec = p.n >> 3;
     const uint64_t stride = (uint64_t)gridDim.x * kThreads;
-    for (uint64_t base = (uint64_t)blockIdx.x * kThreads + threadIdx.x; base < nvec;
-         base += stride * U) {
+    uint64_t base = (uint64_t)blockIdx.x * kThreads + threadIdx.x;
+    for (; base + stride * (U - 1) < nvec; base += stride * U) {
         uint4 q[U];
 #pragma unroll
-        for (int u = 0; u < U; ++u) {
-            const uint64_t i = base + u * stride;
-            q[u] = i < nvec ? ld_keep(g + i) : make_uint4(0, 0, 0, 0);
-        }
+        for (int u = 0; u < U; ++u) q[u] = ld_keep(g + base + u * stride);
 #pragma unroll
-        for (int u = 0; u < U; ++u) {
-            const uint64_t i = base + u * stride;
-            if (i < nvec) p1_consume(a, q[u], i, sc, p);
-        }
+        for (int u = 0; u < U; ++u) p1_consume<KEEP, POW2>(a, q[u], base + u * stride, sc, p);
     }
+    uint4 q[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+        const uint64_t i = base + u * stride;
+        q[u] = i < nvec ? ld_keep(g + i) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+        const uint64_t i = base + u * stride;
+        if (i < nvec) p1_consume<KEEP, POW2>(a, q[u], i, sc, p);
+    }
+}
+
+// KEEP: the compat kept range is non-empty (chosen on the host).
+template <int U, int MINB, bool KEEP>
+__global__ void __launch_bounds__(kThreads, MINB) pass1_kernel(StepParams p) {
+    const P1Scale sc = p1_scale(p);
+    P1Acc a;
+    if (sc.pow2) p1_stream<U, KEEP, true>(a, sc, p);
+    else p1_stream<U, KEEP, false>(a, sc, p);
     if (blockIdx.x == 0 && threadIdx.x < (p.n & 7u)) {   // ragged tail (n % 8)
-        const uint64_t i = (nvec << 3) + threadIdx.x;
+        const uint64_t i = (p.n & ~7ull) + threadIdx.x;
         p1_consume1(a, p.g16[i], i, sc, p);
     }
     p1_finish(a, sc, false, p);
@@ -380,7 +419,7 @@ __global__ void __launch_bounds__(kThreads, MINB) pass1_reduce_kernel(StepParams
                     for (int k = 0; k < 4; ++k) w[k] = pack16(f2h(acc[u][2 * k]), f2h(acc[u][2 * k + 1]));
                     const uint4 rq = make_uint4(w[0], w[1], w[2], w[3]);
                     out[i] = rq;
-                    p1_consume(a, rq, i, sc, p);
+                    p1_consume_any<true>(a, rq, i, sc, p);
                 }
             }
         }
@@ -622,7 +661,7 @@ __global__ void __launch_bounds__(kThreads, MINB) pass1_reduce_nr_kernel(StepPar
                 for (int k = 0; k < 4; ++k) w[k] = pack16(f2h(acc[2 * k]), f2h(acc[2 * k + 1]));
                 const uint4 rq = make_uint4(w[0], w[1], w[2], w[3]);
                 out[i] = rq;
-                p1_consume(a, rq, i, sc, p);
+                p1_consume_any<true>(a, rq, i, sc, p);
             }
         }
         if (blockIdx.x == 0 && threadIdx.x < (p.n & 7u)) {   // ragged tail (n % 8)
@@ -642,19 +681,18 @@ using Pass1Fn = void (*)(StepParams);
 using Pass2Fn = void (*)(StepParams, uint16_t*, float*, float*);
 struct Pass1Variant {
     int unroll, min_blocks;
-    Pass1Fn fn;
+    Pass1Fn fn, fn_keep;   // empty / non-empty compat kept range
 };
 struct Pass2Variant {
     int unroll, min_blocks;
     Pass2Fn fn, fn_w32;    // plain / also writing the FP32 weight copy
 };
+#define ARK_P1(U, B) {U, B, pass1_kernel<U, B, false>, pass1_kernel<U, B, true>}
 static const Pass1Variant kPass1Variants[] = {
-    {4, 4, pass1_kernel<4, 4>},
-    {4, 6, pass1_kernel<4, 6>},
-    {2, 8, pass1_kernel<2, 8>},
-    {8, 4, pass1_kernel<8, 4>},
-    {16, 2, pass1_kernel<16, 2>},
+    ARK_P1(4, 4), ARK_P1(4, 6), ARK_P1(2, 8), ARK_P1(8, 4), ARK_P1(16, 2), ARK_P1(8, 3),
+    ARK_P1(6, 4), ARK_P1(12, 3),
 };
+#undef ARK_P1
 // reduce-scatter pass 1 by rank count (any other count: the generic kernel)
 static Pass1Fn pass1_reduce_for(int world) {
     switch (world) {
@@ -1020,7 +1058,9 @@ int ark_cuda_opt_init(const ark_opt_cfg* cfg, ark_opt_state** out) {
     int var = 3;   // 8 vectors in flight x 4 blocks/SM: fastest on B200 (EKO sweep)
     if (const char* e = getenv("ARK_PASS1_VARIANT")) var = atoi(e);
     if (var < 0 || var >= (int)(sizeof(kPass1Variants) / sizeof(kPass1Variants[0]))) var = 3;
-    s->pass1 = kPass1Variants[var].fn;
+    const bool keep = (cfg->flags & ARK_OPT_COMPAT_GAMMA_FINAL_UNSCALED) &&
+                      cfg->keep_scaled_hi > cfg->keep_scaled_lo;
+    s->pass1 = keep ? kPass1Variants[var].fn_keep : kPass1Variants[var].fn;
     s->blocks1 = streaming_grid(reinterpret_cast<const void*>(s->pass1), kThreads, 0,
                                 (cfg->n >> 3) / kPass1Variants[var].unroll + 1);
     // pass 2: 2 groups in flight x 2 blocks/SM (<= 128 registers) for large

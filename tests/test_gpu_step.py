@@ -131,6 +131,41 @@ def test_early_stop(oracle):
     assert st["consecutive_nans"] == 4 and st["opt_step"] == 0
 
 
+@pytest.mark.parametrize("scale0", [1000.0, 3.0 * 2.0 ** 10])
+def test_non_power_of_two_scale(oracle, scale0):
+    """A loss scale that is not a power of two takes the general unscale
+    path (fp32(h) * inv rounded in f32 as the reference does, FP16 bit
+    patterns checked for inf/NaN); backoff keeps it non-power-of-two."""
+    st, _ = run_steps(oracle, tiny(), steps=5, scale0=scale0, inject={2: 0x7C00, 4: 0xFE00})
+    assert st["skipped_steps"] == 2 and st["opt_step"] == 3
+
+
+@pytest.mark.parametrize("scale0", [65536.0, 1000.0])
+def test_nonfinite_positions(scale0):
+    """The overflow flag for one inf/NaN (or largest finite) value at the
+    first element, inside the first vector, mid-array, in the last whole
+    vector and in the ragged tail; power-of-two and general scale paths."""
+    n = 2048 * 296 + 8 * 3 + 5
+    opt = ab.Optimizer(layout.flat_layout(n), constant_lr=True,
+                       scale=ab.LossScaleConfig(init=scale0, min=2.0 ** -20, max=2.0 ** 24))
+    w16, g16, m, v = synth.make_state(n, 0, 7, "cuda", loss_scale=1.0)
+    gi = g16.view(torch.int16)
+    clean = gi.clone()
+    cases = [(0x7C00, 1), (0xFC00, 1), (0x7E01, 1), (0xFFFF, 1), (0x7BFF, 0), (0xFBFF, 0),
+             (0x0001, 0)]
+    skipped = 0
+    for pos in (0, 7, n // 2, n - 6, n - 1):
+        for val, bad in cases:
+            gi.copy_(clean)
+            gi[pos] = int(np.uint16(val).view(np.int16))
+            opt.step_all(w16, g16, m, v)
+            st = opt.status()
+            assert st["last_overflow"] == bad, (pos, hex(val))
+            skipped += bad
+            assert st["skipped_steps"] == skipped
+    opt.close()
+
+
 def test_eko_full_step_bit_exact(oracle):
     """EKO-237M full optimizer step, t = 1000, scale 65536."""
     st, ost = run_steps(oracle, layout.eko_layout(), steps=1, initial_step=999, fresh_grads=False)
