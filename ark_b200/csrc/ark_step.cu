@@ -296,7 +296,19 @@ __device__ void p1_finish(const P1Acc& a, const P1Scale& sc, bool failed, const 
 // The grid-stride stream of pass 1: rounds of U vectors per thread, loads
 // issued before any is consumed; rounds entirely in range run without
 // per-vector bounds checks, and the one partial round after them with.
-template <int U, bool KEEP, bool POW2>
+// LD 0: L2 only (ld.global.cg); LD 1: the non-coherent path without L1
+// allocation (the gradients are read-only while pass 1 runs).
+template <int LD>
+__device__ __forceinline__ uint4 p1_load(const uint4* p) {
+    if (LD == 0) return ld_keep(p);
+    uint4 r;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+                 : "l"(p));
+    return r;
+}
+
+template <int U, bool KEEP, bool POW2, int LD>
 __device__ __forceinline__ void p1_stream(P1Acc& a, const P1Scale& sc, const StepParams& p) {
     const uint4* g = reinterpret_cast<const uint4*>(p.g16);
     const uint64_t nvec = p.n >> 3;
@@ -305,7 +317,7 @@ __device__ __forceinline__ void p1_stream(P1Acc& a, const P1Scale& sc, const Ste
     for (; base + stride * (U - 1) < nvec; base += stride * U) {
         uint4 q[U];
 #pragma unroll
-        for (int u = 0; u < U; ++u) q[u] = ld_keep(g + base + u * stride);
+        for (int u = 0; u < U; ++u) q[u] = p1_load<LD>(g + base + u * stride);
 #pragma unroll
         for (int u = 0; u < U; ++u) p1_consume<KEEP, POW2>(a, q[u], base + u * stride, sc, p);
     }
@@ -313,7 +325,7 @@ __device__ __forceinline__ void p1_stream(P1Acc& a, const P1Scale& sc, const Ste
 #pragma unroll
     for (int u = 0; u < U; ++u) {
         const uint64_t i = base + u * stride;
-        q[u] = i < nvec ? ld_keep(g + i) : make_uint4(0, 0, 0, 0);
+        q[u] = i < nvec ? p1_load<LD>(g + i) : make_uint4(0, 0, 0, 0);
     }
 #pragma unroll
     for (int u = 0; u < U; ++u) {
@@ -323,12 +335,13 @@ __device__ __forceinline__ void p1_stream(P1Acc& a, const P1Scale& sc, const Ste
 }
 
 // KEEP: the compat kept range is non-empty (chosen on the host).
-template <int U, int MINB, bool KEEP>
+template <int U, int MINB, bool KEEP, int LD>
 __global__ void __launch_bounds__(kThreads, MINB) pass1_kernel(StepParams p) {
+    griddep_launch_dependents();
     const P1Scale sc = p1_scale(p);
     P1Acc a;
-    if (sc.pow2) p1_stream<U, KEEP, true>(a, sc, p);
-    else p1_stream<U, KEEP, false>(a, sc, p);
+    if (sc.pow2) p1_stream<U, KEEP, true, LD>(a, sc, p);
+    else p1_stream<U, KEEP, false, LD>(a, sc, p);
     if (blockIdx.x == 0 && threadIdx.x < (p.n & 7u)) {   // ragged tail (n % 8)
         const uint64_t i = (p.n & ~7ull) + threadIdx.x;
         p1_consume1(a, p.g16[i], i, sc, p);
@@ -379,6 +392,7 @@ __device__ bool reduce_ready_barrier(const StepParams& p) {
 
 template <int U, int MINB>
 __global__ void __launch_bounds__(kThreads, MINB) pass1_reduce_kernel(StepParams p) {
+    griddep_launch_dependents();
     const bool failed = reduce_ready_barrier(p);
     const P1Scale sc = p1_scale(p);
     P1Acc a;
@@ -442,14 +456,27 @@ struct Plan {
     double sumsq;
     uint32_t t;
     int skip;       // overflow, early stop or error: no element work
+    int early_stop;
     int clip;
     int overflow;
     int error;      // ARK_E_* raised while forming the plan (0 = none)
 };
 
-// The step plan from the device state and every rank's {sum, non-finite}.
-__device__ void make_plan(const StepParams& p, Plan& pl) {
+// The step plan, in two parts.  plan_from_state reads only the state (last
+// written by the previous step's pass 2) and the lr table, so pass 2 may
+// form it before pass 1 of this step has completed; plan_from_partials reads
+// every rank's {sum, non-finite}, which pass 1 writes.
+__device__ void plan_from_state(const StepParams& p, Plan& pl) {
     const ark_opt_status st = *p.st;
+    pl.early_stop = st.early_stop != 0;
+    pl.inv = __fdiv_rn(1.0f, st.loss_scale);          // training.rs:244
+    pl.t = st.opt_step + 1u;                          // optimizer.rs:172
+    const uint32_t li = pl.t < p.lr_len ? pl.t : p.lr_len - 1u;
+    pl.lr = p.lr_table[li];                           // optimizer.rs:173
+    pl.k = adam_scalars(pl.lr, p.beta1, p.beta2, p.eps, p.wd, pl.t);
+}
+
+__device__ void plan_from_partials(const StepParams& p, Plan& pl) {
     double sumsq = 0.0;
     unsigned long long bad = 0;
     bool timeout = false;
@@ -464,15 +491,10 @@ __device__ void make_plan(const StepParams& p, Plan& pl) {
     pl.sumsq = sumsq;
     pl.overflow = bad != 0;
     pl.error = timeout ? ARK_E_TIMEOUT : 0;
-    pl.skip = pl.overflow || st.early_stop || timeout;
-    pl.inv = __fdiv_rn(1.0f, st.loss_scale);          // training.rs:244
-    pl.t = st.opt_step + 1u;                          // optimizer.rs:172
-    const uint32_t li = pl.t < p.lr_len ? pl.t : p.lr_len - 1u;
-    pl.lr = p.lr_table[li];                           // optimizer.rs:173
+    pl.skip = pl.overflow || pl.early_stop || timeout;
     pl.norm = __double2float_rn(__dsqrt_rn(sumsq));   // optimizer.rs:145
     pl.clip = (pl.norm > p.clip) && (pl.norm > 0.0f); // optimizer.rs:148
     pl.s = pl.clip ? __fdiv_rn(p.clip, pl.norm) : 1.0f;
-    pl.k = adam_scalars(pl.lr, p.beta1, p.beta2, p.eps, p.wd, pl.t);
 }
 
 // State machine update (training.rs:293-305 on overflow, :316-326 after a
@@ -542,9 +564,77 @@ __device__ __forceinline__ void update8(uint4& wq, const uint4 gq, float4& m0, f
     v1 = make_float4(vv[4], vv[5], vv[6], vv[7]);
 }
 
+// One round of pass 2: U vectors per thread, all loads before any update.
+template <int U>
+struct P2Round {
+    uint4 gq[U], wq[U];
+    float4 ma[U], mb[U], va[U], vb[U];
+};
+
+template <int U>
+__device__ __forceinline__ void p2_load(P2Round<U>& r, uint64_t base, uint64_t stride,
+                                        uint64_t nvec, const uint4* g4, const uint4* w4,
+                                        const float4* m4, const float4* v4, bool with_g) {
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+        const uint64_t j = base + u * stride;
+        if (j < nvec) {
+            const uint64_t i = nvec - 1 - j;
+            if (with_g) r.gq[u] = ld_stream(g4 + i);
+            r.wq[u] = ld_stream(w4 + i);
+            r.ma[u] = ld_stream(m4 + 2 * i);
+            r.mb[u] = ld_stream(m4 + 2 * i + 1);
+            r.va[u] = ld_stream(v4 + 2 * i);
+            r.vb[u] = ld_stream(v4 + 2 * i + 1);
+        }
+    }
+}
+
+template <int U>
+__device__ __forceinline__ void p2_load_g(P2Round<U>& r, uint64_t base, uint64_t stride,
+                                          uint64_t nvec, const uint4* g4) {
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+        const uint64_t j = base + u * stride;
+        if (j < nvec) r.gq[u] = ld_stream(g4 + (nvec - 1 - j));
+    }
+}
+
+template <int U, bool kW32>
+__device__ __forceinline__ void p2_update(P2Round<U>& r, uint64_t base, uint64_t stride,
+                                          uint64_t nvec, uint4* w4, float4* m4, float4* v4,
+                                          const Plan& pl, const StepParams& p) {
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+        const uint64_t j = base + u * stride;
+        if (j < nvec) {
+            const uint64_t i = nvec - 1 - j;
+            update8(r.wq[u], r.gq[u], r.ma[u], r.mb[u], r.va[u], r.vb[u], p.offset + (i << 3),
+                    pl, p);
+            st_stream(w4 + i, r.wq[u]);
+            if (kW32) {   // the forward's FP32 weights (training.rs:165-186)
+                float4* o = reinterpret_cast<float4*>(p.w32_out) + 2 * i;
+                const uint4 wq = r.wq[u];
+                st_stream(o, make_float4(h2f(lo16(wq.x)), h2f(hi16(wq.x)), h2f(lo16(wq.y)),
+                                         h2f(hi16(wq.y))));
+                st_stream(o + 1, make_float4(h2f(lo16(wq.z)), h2f(hi16(wq.z)), h2f(lo16(wq.w)),
+                                             h2f(hi16(wq.w))));
+            }
+            st_stream(m4 + 2 * i, r.ma[u]);
+            st_stream(m4 + 2 * i + 1, r.mb[u]);
+            st_stream(v4 + 2 * i, r.va[u]);
+            st_stream(v4 + 2 * i + 1, r.vb[u]);
+        }
+    }
+}
+
 // Grid-stride over 8-element vectors in reverse (vector i = nvec-1-j for the
 // j-th in forward order): consecutive threads still touch consecutive
 // vectors, and the first vectors updated are the last ones pass 1 read.
+// Launched as a programmatic dependent of pass 1, the blocks start as pass
+// 1's retire: before griddep_wait they form the state part of the plan and
+// load their first round of w, m, v (and g, unless pass 1 writes it: the
+// reduce-scatter step), none of which pass 1 writes.
 template <int kUnroll2, int MINB, bool kW32>
 __global__ void __launch_bounds__(kThreads, MINB) pass2_kernel(StepParams p,
                                                               uint16_t* __restrict__ w16,
@@ -552,53 +642,28 @@ __global__ void __launch_bounds__(kThreads, MINB) pass2_kernel(StepParams p,
                                                               float* __restrict__ v) {
     __shared__ Plan s_plan;
     __shared__ int s_last;
-    if (threadIdx.x == 0) make_plan(p, s_plan);
+    const uint4* g4 = reinterpret_cast<const uint4*>(p.g16);
+    uint4* w4 = reinterpret_cast<uint4*>(w16);
+    float4* m4 = reinterpret_cast<float4*>(m);
+    float4* v4 = reinterpret_cast<float4*>(v);
+    const uint64_t nvec = p.n >> 3;
+    const uint64_t stride = (uint64_t)gridDim.x * kThreads;
+    const bool g_early = p.g16_out == nullptr;
+    uint64_t base = (uint64_t)blockIdx.x * kThreads + threadIdx.x;
+    if (threadIdx.x == 0) plan_from_state(p, s_plan);
+    P2Round<kUnroll2> r;
+    p2_load<kUnroll2>(r, base, stride, nvec, g4, w4, m4, v4, g_early);
+    griddep_wait();
+    if (threadIdx.x == 0) plan_from_partials(p, s_plan);
     __syncthreads();
     const Plan pl = s_plan;
     if (!pl.skip) {
-        const uint4* g4 = reinterpret_cast<const uint4*>(p.g16);
-        uint4* w4 = reinterpret_cast<uint4*>(w16);
-        float4* m4 = reinterpret_cast<float4*>(m);
-        float4* v4 = reinterpret_cast<float4*>(v);
-        const uint64_t nvec = p.n >> 3;
-        const uint64_t stride = (uint64_t)gridDim.x * kThreads;
-        for (uint64_t base = (uint64_t)blockIdx.x * kThreads + threadIdx.x; base < nvec;
-             base += stride * kUnroll2) {
-            uint4 gq[kUnroll2], wq[kUnroll2];
-            float4 ma[kUnroll2], mb[kUnroll2], va[kUnroll2], vb[kUnroll2];
-#pragma unroll
-            for (int u = 0; u < kUnroll2; ++u) {
-                const uint64_t j = base + u * stride;
-                if (j < nvec) {
-                    const uint64_t i = nvec - 1 - j;
-                    gq[u] = ld_stream(g4 + i);
-                    wq[u] = ld_stream(w4 + i);
-                    ma[u] = ld_stream(m4 + 2 * i);
-                    mb[u] = ld_stream(m4 + 2 * i + 1);
-                    va[u] = ld_stream(v4 + 2 * i);
-                    vb[u] = ld_stream(v4 + 2 * i + 1);
-                }
-            }
-#pragma unroll
-            for (int u = 0; u < kUnroll2; ++u) {
-                const uint64_t j = base + u * stride;
-                if (j < nvec) {
-                    const uint64_t i = nvec - 1 - j;
-                    update8(wq[u], gq[u], ma[u], mb[u], va[u], vb[u], p.offset + (i << 3), pl, p);
-                    st_stream(w4 + i, wq[u]);
-                    if (kW32) {   // the forward's FP32 weights (training.rs:165-186)
-                        float4* o = reinterpret_cast<float4*>(p.w32_out) + 2 * i;
-                        st_stream(o, make_float4(h2f(lo16(wq[u].x)), h2f(hi16(wq[u].x)),
-                                                 h2f(lo16(wq[u].y)), h2f(hi16(wq[u].y))));
-                        st_stream(o + 1, make_float4(h2f(lo16(wq[u].z)), h2f(hi16(wq[u].z)),
-                                                     h2f(lo16(wq[u].w)), h2f(hi16(wq[u].w))));
-                    }
-                    st_stream(m4 + 2 * i, ma[u]);
-                    st_stream(m4 + 2 * i + 1, mb[u]);
-                    st_stream(v4 + 2 * i, va[u]);
-                    st_stream(v4 + 2 * i + 1, vb[u]);
-                }
-            }
+        if (!g_early) p2_load_g<kUnroll2>(r, base, stride, nvec, g4);
+        while (base < nvec) {
+            p2_update<kUnroll2, kW32>(r, base, stride, nvec, w4, m4, v4, pl, p);
+            base += stride * kUnroll2;
+            if (base >= nvec) break;
+            p2_load<kUnroll2>(r, base, stride, nvec, g4, w4, m4, v4, true);
         }
         if (blockIdx.x == 0 && threadIdx.x < (p.n & 7u)) {
             const uint64_t i = (nvec << 3) + threadIdx.x;
@@ -622,6 +687,7 @@ __global__ void __launch_bounds__(kThreads, MINB) pass2_kernel(StepParams p,
 // flight before any addition (remote loads over NVLink have long latency).
 template <int NR, int U, int MINB>
 __global__ void __launch_bounds__(kThreads, MINB) pass1_reduce_nr_kernel(StepParams p) {
+    griddep_launch_dependents();
     const bool failed = reduce_ready_barrier(p);
     const P1Scale sc = p1_scale(p);
     P1Acc a;
@@ -687,10 +753,10 @@ struct Pass2Variant {
     int unroll, min_blocks;
     Pass2Fn fn, fn_w32;    // plain / also writing the FP32 weight copy
 };
-#define ARK_P1(U, B) {U, B, pass1_kernel<U, B, false>, pass1_kernel<U, B, true>}
+#define ARK_P1(U, B, L) {U, B, pass1_kernel<U, B, false, L>, pass1_kernel<U, B, true, L>}
 static const Pass1Variant kPass1Variants[] = {
-    ARK_P1(4, 4), ARK_P1(4, 6), ARK_P1(2, 8), ARK_P1(8, 4), ARK_P1(16, 2), ARK_P1(8, 3),
-    ARK_P1(6, 4), ARK_P1(12, 3),
+    ARK_P1(4, 4, 0), ARK_P1(4, 6, 0), ARK_P1(2, 8, 0), ARK_P1(8, 4, 0), ARK_P1(16, 2, 0),
+    ARK_P1(6, 6, 0), ARK_P1(8, 4, 1), ARK_P1(4, 6, 1), ARK_P1(8, 8, 1), ARK_P1(4, 8, 1),
 };
 #undef ARK_P1
 // reduce-scatter pass 1 by rank count (any other count: the generic kernel)
@@ -736,6 +802,7 @@ struct ark_opt_state {
     int blocks1 = 0, blocks2 = 0, blocks1r = 0;
     Pass1Fn pass1 = nullptr, pass1r = nullptr;   // chosen launch-shape variants
     Pass2Fn pass2 = nullptr, pass2_w32 = nullptr;
+    bool pdl = false;  // pass 2 launched as a programmatic dependent of pass 1
     int blocks2w = 0;
     // P2P exchange slots (world > 1)
     bool p2p = false;
@@ -940,6 +1007,23 @@ StepParams make_params(const ark_opt_state* s, const uint16_t* g16) {
     ARK_CUDA_TRY(capturing ? cudaEventRecordWithFlags((e), (st), cudaEventRecordExternal) \
                            : cudaEventRecord((e), (st)))
 
+// Pass 2, as a programmatic dependent of pass 1 when `pdl` (it then directly
+// follows pass 1 in the stream: no event record or collective between).
+cudaError_t launch_pass2(Pass2Fn fn, int blocks, cudaStream_t stream, bool pdl,
+                         const StepParams& p, uint16_t* w16, float* m, float* v) {
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3((unsigned)blocks);
+    lc.blockDim = dim3(kThreads);
+    lc.dynamicSmemBytes = 0;
+    lc.stream = stream;
+    lc.attrs = attr;
+    lc.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&lc, fn, p, w16, m, v);
+}
+
 int enqueue_step(ark_opt_state* s, cudaStream_t stream, uint16_t* w16, const uint16_t* g16,
                  float* m, float* v, float* w32, cudaEvent_t* ev, bool capturing = false,
                  bool reduce = false) {
@@ -960,9 +1044,9 @@ int enqueue_step(ark_opt_state* s, cudaStream_t stream, uint16_t* w16, const uin
         }
     }
     if (ev) ARK_RECORD(ev[2], stream);
-    if (w32) s->pass2_w32<<<s->blocks2w, kThreads, 0, stream>>>(p, w16, m, v);
-    else s->pass2<<<s->blocks2, kThreads, 0, stream>>>(p, w16, m, v);
-    ARK_CUDA_TRY(cudaGetLastError());
+    const bool pdl = s->pdl && !ev && (s->cfg.world_size == 1 || s->p2p);
+    if (w32) ARK_CUDA_TRY(launch_pass2(s->pass2_w32, s->blocks2w, stream, pdl, p, w16, m, v));
+    else ARK_CUDA_TRY(launch_pass2(s->pass2, s->blocks2, stream, pdl, p, w16, m, v));
     if (ev) ARK_RECORD(ev[3], stream);
     return ARK_OK;
 }
@@ -1054,10 +1138,20 @@ int ark_cuda_opt_init(const ark_opt_cfg* cfg, ark_opt_state** out) {
     // The caller's stream (NULL: the legacy default stream), so the step is
     // ordered after whatever produced the gradients on that stream.
     s->stream = reinterpret_cast<cudaStream_t>(cfg->stream);
-    // pass-1 variant: vectors in flight per thread x resident blocks per SM
-    int var = 3;   // 8 vectors in flight x 4 blocks/SM: fastest on B200 (EKO sweep)
+    // pass-1 variant: vectors in flight per thread x resident blocks per SM x
+    // load path.  B200 sweeps (EKO and EKO/8 shards): 4 x 6 through the
+    // non-coherent path for large shards (pass 2 after it also runs faster:
+    // EKO step 0.912 ms vs 0.926 ms for 8 x 4 through L2-only loads), 4 x 6
+    // L2-only below 100M params
+    const int nvar1 = (int)(sizeof(kPass1Variants) / sizeof(kPass1Variants[0]));
+    int var = cfg->n < 100000000ull ? 1 : 7;
+    // pass 2 as a programmatic dependent of pass 1 below 100M params: its
+    // prologue then overlaps pass 1's tail (B200, EKO/8 shard: 0.1188 vs
+    // 0.1214 ms per step; no gain at the full EKO size)
+    s->pdl = cfg->n < 100000000ull;
+    if (const char* e = getenv("ARK_PDL")) s->pdl = atoi(e) != 0;
     if (const char* e = getenv("ARK_PASS1_VARIANT")) var = atoi(e);
-    if (var < 0 || var >= (int)(sizeof(kPass1Variants) / sizeof(kPass1Variants[0]))) var = 3;
+    if (var < 0 || var >= nvar1) var = 1;
     const bool keep = (cfg->flags & ARK_OPT_COMPAT_GAMMA_FINAL_UNSCALED) &&
                       cfg->keep_scaled_hi > cfg->keep_scaled_lo;
     s->pass1 = keep ? kPass1Variants[var].fn_keep : kPass1Variants[var].fn;

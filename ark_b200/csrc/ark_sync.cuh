@@ -30,4 +30,15 @@ __device__ __forceinline__ void ld_relaxed_sys_v2(const uint64_t* p, uint64_t& a
                  : "memory");
 }
 
+// Programmatic dependent launch (sm_90 and later).  launch_dependents lets
+// the next kernel in the stream, when launched with programmatic stream
+// serialization, start its blocks as this grid's blocks retire; wait, in
+// that next kernel, returns once this grid has completed and its memory
+// operations are visible.  In a kernel launched without the attribute,
+// wait returns at once.
+__device__ __forceinline__ void griddep_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 }  // namespace ark
