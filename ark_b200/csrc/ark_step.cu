@@ -1145,10 +1145,11 @@ int ark_cuda_opt_init(const ark_opt_cfg* cfg, ark_opt_state** out) {
     // L2-only below 100M params
     const int nvar1 = (int)(sizeof(kPass1Variants) / sizeof(kPass1Variants[0]));
     int var = cfg->n < 100000000ull ? 1 : 7;
-    // pass 2 as a programmatic dependent of pass 1 below 100M params: its
-    // prologue then overlaps pass 1's tail (B200, EKO/8 shard: 0.1188 vs
-    // 0.1214 ms per step; no gain at the full EKO size)
-    s->pdl = cfg->n < 100000000ull;
+    // pass 2 as a programmatic dependent of pass 1: its prologue overlaps
+    // pass 1's tail.  B200, ms per step without / with: EKO/8 shard 0.1214 /
+    // 0.1188, EKO/2 shards on 2 GPUs 0.4731 / 0.4717, full EKO 0.9007 /
+    // 0.9018 (within run-to-run spread)
+    s->pdl = true;
     if (const char* e = getenv("ARK_PDL")) s->pdl = atoi(e) != 0;
     if (const char* e = getenv("ARK_PASS1_VARIANT")) var = atoi(e);
     if (var < 0 || var >= nvar1) var = 1;
