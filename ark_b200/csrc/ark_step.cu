@@ -532,6 +532,11 @@ __device__ void advance_state(const StepParams& p, const Plan& pl) {
     *p.st = st;
 }
 
+// Eight elements of the update.  Without KEEP the compat kept range is
+// empty and no element index is compared for it; the weight-decay boundary
+// n_decay is turned into a count of decayed elements in this vector (0-8)
+// once, so each element costs one 32-bit compare.
+template <bool KEEP>
 __device__ __forceinline__ void update8(uint4& wq, const uint4 gq, float4& m0, float4& m1,
                                         float4& v0, float4& v1, uint64_t gi0, const Plan& pl,
                                         const StepParams& p) {
@@ -539,9 +544,9 @@ __device__ __forceinline__ void update8(uint4& wq, const uint4 gq, float4& m0, f
     uint32_t ww[4] = {wq.x, wq.y, wq.z, wq.w};
     float mm[8] = {m0.x, m0.y, m0.z, m0.w, m1.x, m1.y, m1.z, m1.w};
     float vv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-    const bool keep_any = (gi0 + 8 > p.keep_lo) && (gi0 < p.keep_hi);
-    const bool dec_all = gi0 + 8 <= p.n_decay;
-    const bool dec_none = gi0 >= p.n_decay;
+    const bool keep_any = KEEP && (gi0 + 8 > p.keep_lo) && (gi0 < p.keep_hi);
+    const uint32_t ndec = gi0 >= p.n_decay ? 0u
+                          : (p.n_decay - gi0 >= 8 ? 8u : (uint32_t)(p.n_decay - gi0));
     uint16_t wout[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
@@ -551,8 +556,7 @@ __device__ __forceinline__ void update8(uint4& wq, const uint4 gq, float4& m0, f
         const bool keep = keep_any && (gi0 + j >= p.keep_lo) && (gi0 + j < p.keep_hi);
         if (!keep) gf = __fmul_rn(gf, pl.inv);                       // training.rs:308
         if (pl.clip) gf = __fmul_rn(gf, pl.s);                       // optimizer.rs:151-166
-        const bool dec = dec_all || (!dec_none && gi0 + j < p.n_decay);
-        const float decay = dec ? pl.k.decay : 1.0f;                 // wd = 0: 1 - lr*0
+        const float decay = (uint32_t)j < ndec ? pl.k.decay : 1.0f;  // wd = 0: 1 - lr*0
         wout[j] = f2h(adam_elem(h2f(wh), gf, mm[j], vv[j], pl.k, decay));
     }
 #pragma unroll
@@ -600,7 +604,7 @@ __device__ __forceinline__ void p2_load_g(P2Round<U>& r, uint64_t base, uint64_t
     }
 }
 
-template <int U, bool kW32>
+template <int U, bool kW32, bool KEEP>
 __device__ __forceinline__ void p2_update(P2Round<U>& r, uint64_t base, uint64_t stride,
                                           uint64_t nvec, uint4* w4, float4* m4, float4* v4,
                                           const Plan& pl, const StepParams& p) {
@@ -609,8 +613,8 @@ __device__ __forceinline__ void p2_update(P2Round<U>& r, uint64_t base, uint64_t
         const uint64_t j = base + u * stride;
         if (j < nvec) {
             const uint64_t i = nvec - 1 - j;
-            update8(r.wq[u], r.gq[u], r.ma[u], r.mb[u], r.va[u], r.vb[u], p.offset + (i << 3),
-                    pl, p);
+            update8<KEEP>(r.wq[u], r.gq[u], r.ma[u], r.mb[u], r.va[u], r.vb[u],
+                          p.offset + (i << 3), pl, p);
             st_stream(w4 + i, r.wq[u]);
             if (kW32) {   // the forward's FP32 weights (training.rs:165-186)
                 float4* o = reinterpret_cast<float4*>(p.w32_out) + 2 * i;
@@ -635,7 +639,7 @@ __device__ __forceinline__ void p2_update(P2Round<U>& r, uint64_t base, uint64_t
 // 1's retire: before griddep_wait they form the state part of the plan and
 // load their first round of w, m, v (and g, unless pass 1 writes it: the
 // reduce-scatter step), none of which pass 1 writes.
-template <int kUnroll2, int MINB, bool kW32>
+template <int kUnroll2, int MINB, bool kW32, bool KEEP>
 __global__ void __launch_bounds__(kThreads, MINB) pass2_kernel(StepParams p,
                                                               uint16_t* __restrict__ w16,
                                                               float* __restrict__ m,
@@ -660,7 +664,7 @@ __global__ void __launch_bounds__(kThreads, MINB) pass2_kernel(StepParams p,
     if (!pl.skip) {
         if (!g_early) p2_load_g<kUnroll2>(r, base, stride, nvec, g4);
         while (base < nvec) {
-            p2_update<kUnroll2, kW32>(r, base, stride, nvec, w4, m4, v4, pl, p);
+            p2_update<kUnroll2, kW32, KEEP>(r, base, stride, nvec, w4, m4, v4, pl, p);
             base += stride * kUnroll2;
             if (base >= nvec) break;
             p2_load<kUnroll2>(r, base, stride, nvec, g4, w4, m4, v4, true);
@@ -751,7 +755,7 @@ struct Pass1Variant {
 };
 struct Pass2Variant {
     int unroll, min_blocks;
-    Pass2Fn fn, fn_w32;    // plain / also writing the FP32 weight copy
+    Pass2Fn fn[2], fn_w32[2];   // [kept range non-empty]: plain / also writing FP32 weights
 };
 #define ARK_P1(U, B, L) {U, B, pass1_kernel<U, B, false, L>, pass1_kernel<U, B, true, L>}
 static const Pass1Variant kPass1Variants[] = {
@@ -769,13 +773,13 @@ static Pass1Fn pass1_reduce_for(int world) {
         default: return pass1_reduce_kernel<2, 4>;
     }
 }
+#define ARK_P2(U, B)                                                                     \
+    {U, B, {pass2_kernel<U, B, false, false>, pass2_kernel<U, B, false, true>},            \
+     {pass2_kernel<U, B, true, false>, pass2_kernel<U, B, true, true>}}
 static const Pass2Variant kPass2Variants[] = {
-    {2, 1, pass2_kernel<2, 1, false>, pass2_kernel<2, 1, true>},
-    {1, 3, pass2_kernel<1, 3, false>, pass2_kernel<1, 3, true>},
-    {1, 4, pass2_kernel<1, 4, false>, pass2_kernel<1, 4, true>},
-    {3, 1, pass2_kernel<3, 1, false>, pass2_kernel<3, 1, true>},
-    {2, 2, pass2_kernel<2, 2, false>, pass2_kernel<2, 2, true>},
+    ARK_P2(2, 1), ARK_P2(1, 3), ARK_P2(1, 4), ARK_P2(3, 1), ARK_P2(2, 2),
 };
+#undef ARK_P2
 
 }  // namespace ark
 
@@ -1164,13 +1168,13 @@ int ark_cuda_opt_init(const ark_opt_cfg* cfg, ark_opt_state** out) {
     int var2 = cfg->n < 100000000ull ? 1 : 4;
     if (const char* e = getenv("ARK_PASS2_VARIANT")) var2 = atoi(e);
     if (var2 < 0 || var2 >= (int)(sizeof(kPass2Variants) / sizeof(kPass2Variants[0]))) var2 = 0;
-    s->pass2 = kPass2Variants[var2].fn;
+    s->pass2 = kPass2Variants[var2].fn[keep];
     // with the FP32 weight copy: 2 groups x 2 blocks/SM (122 registers) is
     // the fastest shape on B200 (EKO: 1.161 ms vs 1.237 ms for 1 x 3)
     int varw = 4;
     if (const char* e = getenv("ARK_PASS2W_VARIANT")) varw = atoi(e);
     if (varw < 0 || varw >= (int)(sizeof(kPass2Variants) / sizeof(kPass2Variants[0]))) varw = 4;
-    s->pass2_w32 = kPass2Variants[varw].fn_w32;
+    s->pass2_w32 = kPass2Variants[varw].fn_w32[keep];
     s->blocks2w = streaming_grid(reinterpret_cast<const void*>(s->pass2_w32), kThreads, 0,
                                  (cfg->n >> 3) / kPass2Variants[varw].unroll + 1);
     s->pass1r = pass1_reduce_for(cfg->world_size);
