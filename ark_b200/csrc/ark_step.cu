@@ -533,10 +533,11 @@ __device__ void advance_state(const StepParams& p, const Plan& pl) {
 }
 
 // Eight elements of the update.  Without KEEP the compat kept range is
-// empty and no element index is compared for it; the weight-decay boundary
-// n_decay is turned into a count of decayed elements in this vector (0-8)
-// once, so each element costs one 32-bit compare.
-template <bool KEEP>
+// empty and no element index is compared for it.  DEC 1 turns the
+// weight-decay boundary n_decay into a count of decayed elements in this
+// vector (0-8) once, so each element costs one 32-bit compare; DEC 0
+// compares each element's 64-bit index with the boundary.
+template <bool KEEP, int DEC>
 __device__ __forceinline__ void update8(uint4& wq, const uint4 gq, float4& m0, float4& m1,
                                         float4& v0, float4& v1, uint64_t gi0, const Plan& pl,
                                         const StepParams& p) {
@@ -547,6 +548,8 @@ __device__ __forceinline__ void update8(uint4& wq, const uint4 gq, float4& m0, f
     const bool keep_any = KEEP && (gi0 + 8 > p.keep_lo) && (gi0 < p.keep_hi);
     const uint32_t ndec = gi0 >= p.n_decay ? 0u
                           : (p.n_decay - gi0 >= 8 ? 8u : (uint32_t)(p.n_decay - gi0));
+    const bool dec_all = gi0 + 8 <= p.n_decay;
+    const bool dec_none = gi0 >= p.n_decay;
     uint16_t wout[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
@@ -556,7 +559,9 @@ __device__ __forceinline__ void update8(uint4& wq, const uint4 gq, float4& m0, f
         const bool keep = keep_any && (gi0 + j >= p.keep_lo) && (gi0 + j < p.keep_hi);
         if (!keep) gf = __fmul_rn(gf, pl.inv);                       // training.rs:308
         if (pl.clip) gf = __fmul_rn(gf, pl.s);                       // optimizer.rs:151-166
-        const float decay = (uint32_t)j < ndec ? pl.k.decay : 1.0f;  // wd = 0: 1 - lr*0
+        const bool dec = DEC ? (uint32_t)j < ndec
+                             : (dec_all || (!dec_none && gi0 + j < p.n_decay));
+        const float decay = dec ? pl.k.decay : 1.0f;  // wd = 0: 1 - lr*0
         wout[j] = f2h(adam_elem(h2f(wh), gf, mm[j], vv[j], pl.k, decay));
     }
 #pragma unroll
@@ -604,7 +609,7 @@ __device__ __forceinline__ void p2_load_g(P2Round<U>& r, uint64_t base, uint64_t
     }
 }
 
-template <int U, bool kW32, bool KEEP>
+template <int U, bool kW32, bool KEEP, int DEC>
 __device__ __forceinline__ void p2_update(P2Round<U>& r, uint64_t base, uint64_t stride,
                                           uint64_t nvec, uint4* w4, float4* m4, float4* v4,
                                           const Plan& pl, const StepParams& p) {
@@ -613,7 +618,7 @@ __device__ __forceinline__ void p2_update(P2Round<U>& r, uint64_t base, uint64_t
         const uint64_t j = base + u * stride;
         if (j < nvec) {
             const uint64_t i = nvec - 1 - j;
-            update8<KEEP>(r.wq[u], r.gq[u], r.ma[u], r.mb[u], r.va[u], r.vb[u],
+            update8<KEEP, DEC>(r.wq[u], r.gq[u], r.ma[u], r.mb[u], r.va[u], r.vb[u],
                           p.offset + (i << 3), pl, p);
             st_stream(w4 + i, r.wq[u]);
             if (kW32) {   // the forward's FP32 weights (training.rs:165-186)
@@ -639,7 +644,7 @@ __device__ __forceinline__ void p2_update(P2Round<U>& r, uint64_t base, uint64_t
 // 1's retire: before griddep_wait they form the state part of the plan and
 // load their first round of w, m, v (and g, unless pass 1 writes it: the
 // reduce-scatter step), none of which pass 1 writes.
-template <int kUnroll2, int MINB, bool kW32, bool KEEP>
+template <int kUnroll2, int MINB, bool kW32, bool KEEP, int DEC = 1>
 __global__ void __launch_bounds__(kThreads, MINB) pass2_kernel(StepParams p,
                                                               uint16_t* __restrict__ w16,
                                                               float* __restrict__ m,
@@ -664,7 +669,7 @@ __global__ void __launch_bounds__(kThreads, MINB) pass2_kernel(StepParams p,
     if (!pl.skip) {
         if (!g_early) p2_load_g<kUnroll2>(r, base, stride, nvec, g4);
         while (base < nvec) {
-            p2_update<kUnroll2, kW32, KEEP>(r, base, stride, nvec, w4, m4, v4, pl, p);
+            p2_update<kUnroll2, kW32, KEEP, DEC>(r, base, stride, nvec, w4, m4, v4, pl, p);
             base += stride * kUnroll2;
             if (base >= nvec) break;
             p2_load<kUnroll2>(r, base, stride, nvec, g4, w4, m4, v4, true);
@@ -776,9 +781,20 @@ static Pass1Fn pass1_reduce_for(int world) {
 #define ARK_P2(U, B)                                                                     \
     {U, B, {pass2_kernel<U, B, false, false>, pass2_kernel<U, B, false, true>},            \
      {pass2_kernel<U, B, true, false>, pass2_kernel<U, B, true, true>}}
+#define ARK_P2X(U, B, K, D)                                                              \
+    {U, B, {pass2_kernel<U, B, false, K, D>, pass2_kernel<U, B, false, true, D>},          \
+     {pass2_kernel<U, B, true, K, D>, pass2_kernel<U, B, true, true, D>}}
+// 5 and 6: the 2 x 2 shape with the kept-range check compiled in even when
+// the range is empty (5: decay chosen by two 64-bit boundary compares, 6: by
+// the per-vector count).  On B200 these are faster than 4 when the SM clock
+// is not power-capped (EKO step 0.900 vs 0.925 ms at 1965 MHz) and slower
+// when it is (0.918-0.921 vs 0.907 ms at ~1670 MHz, the usual state of a
+// long run under the 1 kW cap), which is why 4 is the default.
 static const Pass2Variant kPass2Variants[] = {
     ARK_P2(2, 1), ARK_P2(1, 3), ARK_P2(1, 4), ARK_P2(3, 1), ARK_P2(2, 2),
+    ARK_P2X(2, 2, true, 0), ARK_P2X(2, 2, true, 1),
 };
+#undef ARK_P2X
 #undef ARK_P2
 
 }  // namespace ark
