@@ -397,16 +397,23 @@ def run_ours(args):
     # per-kernel split is timed in a second region of K steps right after,
     # with event-record nodes between the kernels.  A state below 4x the L2
     # is timed step by step instead, with the L2 flushed between steps.
-    flush = n * STATE_BYTES_PER_PARAM < 4 * L2_BYTES
+    # (decided on the mean shard, so every rank makes the same choice)
+    flush = (L.n // world) * STATE_BYTES_PER_PARAM < 4 * L2_BYTES
     # flush: write 256 MiB (evicts the L2), then read another 256 MiB, so that
     # the dirty flush lines are written back before the step, not during it
     scratch = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=dev) if flush else None
     scratch_r = torch.zeros(FLUSH_BYTES // 4, dtype=torch.float32, device=dev) if flush else None
     sink = torch.empty((), dtype=torch.float32, device=dev)
+    tok = torch.zeros(1, dtype=torch.float32, device=dev)
 
     def flush_l2(k):
         scratch.fill_(float(k))
         torch.sum(scratch_r, dim=0, out=sink)
+        if world > 1:
+            # device-side barrier: every rank's stream passes this point
+            # together, so no rank's step event includes waiting for a peer
+            # that is still flushing
+            dist.all_reduce(tok)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     step_evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                 for _ in range(args.steps)] if flush else []
