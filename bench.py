@@ -195,6 +195,13 @@ def cpu_reference_step_setup(L, threads, n_tensors=None):
     return step
 
 
+def needs_flush(n_total, world):
+    """True when a rank's state (w, g, m, v of the mean shard) is below 4x
+    the L2: such steps are timed one by one with the L2 flushed between
+    them.  Decided on the mean shard so that every rank agrees."""
+    return (n_total // world) * STATE_BYTES_PER_PARAM < 4 * L2_BYTES
+
+
 def bounded_reference_step(L, threads, n_steps, budget_s):
     """A full-EKO step if n_steps of them fit in budget_s, else the longest
     prefix of the reference tensor order that does (a bounded sample)."""
@@ -397,8 +404,7 @@ def run_ours(args):
     # per-kernel split is timed in a second region of K steps right after,
     # with event-record nodes between the kernels.  A state below 4x the L2
     # is timed step by step instead, with the L2 flushed between steps.
-    # (decided on the mean shard, so every rank makes the same choice)
-    flush = (L.n // world) * STATE_BYTES_PER_PARAM < 4 * L2_BYTES
+    flush = needs_flush(L.n, world)
     # flush: write 256 MiB (evicts the L2), then read another 256 MiB, so that
     # the dirty flush lines are written back before the step, not during it
     scratch = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=dev) if flush else None
