@@ -14,11 +14,15 @@
 //   pass 2  every block derives the step plan from device memory: skip on
 //           overflow (training.rs:293-305), else t = step+1, lr(t), clip
 //           coefficient (optimizer.rs:145-149), AdamW scalars
-//           (opti.s:210-271).  Then the fused element update (20 B/param):
-//           g = fp16(g) * inv_scale * clip ; m, v, w as opti.s:285-308,
-//           walking the shard in REVERSE so the gradient lines pass 1 read
-//           last are still in L2.  The last block to finish advances the
-//           loss-scale state machine (training.rs:316-326).
+//           (opti.s:210-271).  Then the fused element update (22 B/param:
+//           g, w, m, v read, w, m, v written): g = fp16(g) * inv_scale *
+//           clip ; m, v, w as opti.s:285-308, walking the shard in REVERSE
+//           so the gradient lines pass 1 read last are still in L2.  The
+//           last block to finish advances the loss-scale state machine
+//           (training.rs:316-326).  Launched as a programmatic dependent of
+//           pass 1: its blocks start as pass 1's retire, form the parts of
+//           the plan that only need the state, load their first vectors,
+//           and wait in the kernel for pass 1's results.
 #include <cuda_runtime.h>
 #include <nccl.h>
 #include <stdlib.h>
