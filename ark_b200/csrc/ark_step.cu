@@ -755,7 +755,11 @@ __global__ void __launch_bounds__(kThreads, MINB) pass1_reduce_nr_kernel(StepPar
     p1_finish(a, sc, failed, p);
 }
 
-// launch-shape variants: vectors in flight per thread x minimum resident blocks
+// Launch-shape variants, selected at init by shard size (or by index through
+// ARK_PASS1_VARIANT / ARK_PASS2_VARIANT / ARK_PASS2W_VARIANT).  Pass 1:
+// vectors in flight per thread x minimum resident blocks per SM x load path
+// (0: L2 only, 1: non-coherent); pass 2: 8-element groups in flight per
+// thread x minimum resident blocks per SM.
 using Pass1Fn = void (*)(StepParams);
 using Pass2Fn = void (*)(StepParams, uint16_t*, float*, float*);
 struct Pass1Variant {
