@@ -1173,14 +1173,14 @@ int ark_cuda_opt_init(const ark_opt_cfg* cfg, ark_opt_state** out) {
     // L2-only below 100M params
     const int nvar1 = (int)(sizeof(kPass1Variants) / sizeof(kPass1Variants[0]));
     int var = cfg->n < 100000000ull ? 1 : 7;
+    if (const char* e = getenv("ARK_PASS1_VARIANT")) var = atoi(e);
+    if (var < 0 || var >= nvar1) var = 1;
     // pass 2 as a programmatic dependent of pass 1: its prologue overlaps
     // pass 1's tail.  B200, ms per step without / with: EKO/8 shard 0.1214 /
     // 0.1188, EKO/2 shards on 2 GPUs 0.4731 / 0.4717, full EKO 0.9007 /
     // 0.9018 (within run-to-run spread)
     s->pdl = true;
     if (const char* e = getenv("ARK_PDL")) s->pdl = atoi(e) != 0;
-    if (const char* e = getenv("ARK_PASS1_VARIANT")) var = atoi(e);
-    if (var < 0 || var >= nvar1) var = 1;
     const bool keep = (cfg->flags & ARK_OPT_COMPAT_GAMMA_FINAL_UNSCALED) &&
                       cfg->keep_scaled_hi > cfg->keep_scaled_lo;
     s->pass1 = keep ? kPass1Variants[var].fn_keep : kPass1Variants[var].fn;
@@ -1193,8 +1193,8 @@ int ark_cuda_opt_init(const ark_opt_cfg* cfg, ark_opt_state** out) {
     if (const char* e = getenv("ARK_PASS2_VARIANT")) var2 = atoi(e);
     if (var2 < 0 || var2 >= (int)(sizeof(kPass2Variants) / sizeof(kPass2Variants[0]))) var2 = 0;
     s->pass2 = kPass2Variants[var2].fn[keep];
-    // with the FP32 weight copy: 2 groups x 2 blocks/SM (122 registers) is
-    // the fastest shape on B200 (EKO: 1.161 ms vs 1.237 ms for 1 x 3)
+    // with the FP32 weight copy: 2 groups x 2 blocks/SM (<= 128 registers)
+    // is the fastest shape on B200 (EKO: 1.161 ms vs 1.237 ms for 1 x 3)
     int varw = 4;
     if (const char* e = getenv("ARK_PASS2W_VARIANT")) varw = atoi(e);
     if (varw < 0 || varw >= (int)(sizeof(kPass2Variants) / sizeof(kPass2Variants[0]))) varw = 4;
