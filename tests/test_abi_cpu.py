@@ -1,6 +1,7 @@
 """C-ABI checks that need no GPU: the library loads, exports every symbol
 include/ark_opt.h declares, its structs match the ctypes mirrors, and the
 host-only lr schedule equals the oracle's restatement of lr_now."""
+import ctypes
 import os
 import re
 import subprocess
@@ -101,3 +102,40 @@ def build_c_example(tmp_path):
 def test_plain_c_caller_compiles_and_links(tmp_path):
     """The header is plain C and the library links from a C program."""
     assert build_c_example(tmp_path).exists()
+
+
+def _valid_cfg(table):
+    cfg = _lib.OptCfg()
+    cfg.abi_version = 2
+    cfg.n = 1024
+    cfg.n_decay = 1024
+    cfg.lr_table = table
+    cfg.lr_table_len = 1
+    cfg.beta1, cfg.beta2, cfg.eps, cfg.weight_decay, cfg.grad_clip = 0.9, 0.95, 1e-8, 0.1, 1.0
+    cfg.scale_init, cfg.scale_backoff, cfg.scale_growth = 65536.0, 0.5, 2.0
+    cfg.scale_min, cfg.scale_max, cfg.scale_every, cfg.max_consecutive_nans = 1.0, 2.0 ** 24, 50, 200
+    cfg.world_size = 1
+    return cfg
+
+
+def test_init_reports_errors_without_touching_a_gpu():
+    """The error channel of ark_cuda_opt_init: a bad config is rejected
+    before any CUDA call; a valid one on a machine without a usable device
+    returns ARK_E_NO_DEVICE and leaves the handle NULL (no crash, no
+    abort)."""
+    import torch
+    L = _lib.lib()
+    table = (ctypes.c_float * 1)(3e-4)
+    h = ctypes.c_void_p(1)
+    assert L.ark_cuda_opt_init(None, ctypes.byref(h)) == -1
+    bad = _valid_cfg(table)
+    bad.abi_version = 1
+    assert L.ark_cuda_opt_init(ctypes.byref(bad), ctypes.byref(h)) == -1
+    bad = _valid_cfg(table)
+    bad.lr_table_len = 0
+    assert L.ark_cuda_opt_init(ctypes.byref(bad), ctypes.byref(h)) == -1
+    if torch.cuda.is_available():
+        return
+    rc = L.ark_cuda_opt_init(ctypes.byref(_valid_cfg(table)), ctypes.byref(h))
+    assert rc == -7 and not h.value
+    assert L.ark_cuda_strerror(-7)
