@@ -26,6 +26,7 @@ ARK_OPT_COMPAT_GAMMA_FINAL_UNSCALED = 0x1
 ARK_OPT_USE_GRAPH = 0x2
 ARK_OPT_NCCL_EXCHANGE = 0x4
 ARK_STEP_REDUCE = 0x1
+ARK_STEP_GATHER_WEIGHTS = 0x2
 ARK_CKPT_RESTORE_SCALE = 0x1
 
 c_f, c_u32, c_u64, c_i, c_i32, c_d, c_p = (ctypes.c_float, ctypes.c_uint32, ctypes.c_uint64,
@@ -85,6 +86,10 @@ SIGNATURES = {
     "ark_cuda_opt_grad_buffer": (c_i, [c_p, c_u64, ctypes.POINTER(c_p)]),
     "ark_cuda_opt_step_reduce": (c_i, [c_p, c_p, c_p, c_p, c_p]),
     "ark_cuda_opt_step_ex": (c_i, [c_p, c_p, c_p, c_p, c_p, c_p, c_u32]),
+    "ark_cuda_opt_weight_buffer": (c_i, [c_p, c_u64, ctypes.POINTER(c_p)]),
+    "ark_cuda_opt_weights_wait": (c_i, [c_p]),
+    "ark_cuda_opt_logits_check": (c_i, [c_p, c_p, c_u64]),
+    "ark_cuda_opt_zero_grads": (c_i, [c_p]),
     "ark_cuda_opt_read_status": (c_i, [c_p, ctypes.POINTER(OptStatus)]),
     "ark_cuda_opt_set_status": (c_i, [c_p, ctypes.POINTER(OptStatus)]),
     "ark_cuda_opt_upload_grads": (c_i, [c_p, c_p, c_p, c_u64]),

@@ -53,13 +53,41 @@ const char* status_string(int s) {
     }
 }
 
-int streaming_grid(const void* kernel, int threads, size_t dyn_smem, uint64_t work_items) {
-    int dev = 0, sms = 148, per_sm = 1;
+// Resident-block capacity (SMs x blocks per SM) per kernel and device,
+// looked up once: the legacy entry points are called hundreds of times per
+// optimizer step (one call per tensor), and the occupancy query costs more
+// host time than launching a small kernel.
+struct GridCacheEntry {
+    const void* kernel;
+    int dev, threads;
+    size_t smem;
+    uint64_t full;
+};
+static std::mutex g_grid_mu;
+static GridCacheEntry g_grid_cache[128];
+static int g_grid_used = 0;
+
+static uint64_t resident_capacity(const void* kernel, int threads, size_t dyn_smem) {
+    int dev = 0;
     cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lk(g_grid_mu);
+    for (int i = 0; i < g_grid_used; ++i) {
+        const GridCacheEntry& e = g_grid_cache[i];
+        if (e.kernel == kernel && e.dev == dev && e.threads == threads && e.smem == dyn_smem)
+            return e.full;
+    }
+    int sms = 148, per_sm = 1;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, dyn_smem);
     if (per_sm < 1) per_sm = 1;
-    uint64_t full = (uint64_t)sms * (uint64_t)per_sm;
+    const uint64_t full = (uint64_t)sms * (uint64_t)per_sm;
+    if (g_grid_used < (int)(sizeof(g_grid_cache) / sizeof(g_grid_cache[0])))
+        g_grid_cache[g_grid_used++] = GridCacheEntry{kernel, dev, threads, dyn_smem, full};
+    return full;
+}
+
+int streaming_grid(const void* kernel, int threads, size_t dyn_smem, uint64_t work_items) {
+    const uint64_t full = resident_capacity(kernel, threads, dyn_smem);
     uint64_t need = (work_items + threads - 1) / threads;
     if (need < 1) need = 1;
     return (int)(need < full ? need : full);
@@ -179,6 +207,91 @@ __global__ void __launch_bounds__(kT) adam_vec_kernel(WT* __restrict__ w, const 
     }
 }
 
+// Main vector path (every pointer 16-byte aligned): 8-element groups, U of
+// them per thread per round, every load of a round issued before the first
+// update -- g, m, v as two float4 each and w as one 16-byte vector of halves
+// (or two float4).  Launch bounds keep it at <= 128 registers (2 blocks of
+// 256 per SM), the shape of the fused step's update kernel.
+template <typename WT, int U>
+__global__ void __launch_bounds__(kT, 2) adam_vec8_kernel(WT* __restrict__ w,
+                                                         const float* __restrict__ g,
+                                                         float* __restrict__ m,
+                                                         float* __restrict__ v, AdamArgs a) {
+    __shared__ AdamK s_k;
+    if (threadIdx.x == 0) s_k = adam_scalars(a.lr, a.b1, a.b2, a.eps, a.wd, a.t);
+    __syncthreads();
+    const AdamK k = s_k;
+    const uint64_t n8 = a.n >> 3;
+    const uint64_t stride = (uint64_t)gridDim.x * kT;
+    const float4* g4 = reinterpret_cast<const float4*>(g);
+    float4* m4 = reinterpret_cast<float4*>(m);
+    float4* v4 = reinterpret_cast<float4*>(v);
+    for (uint64_t base = (uint64_t)blockIdx.x * kT + threadIdx.x; base < n8;
+         base += stride * U) {
+        float4 gq[U][2], mq[U][2], vq[U][2], wq[U][2];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const uint64_t i = base + u * stride;
+            if (i < n8) {
+                gq[u][0] = ld_stream(g4 + 2 * i);
+                gq[u][1] = ld_stream(g4 + 2 * i + 1);
+                mq[u][0] = ld_stream(m4 + 2 * i);
+                mq[u][1] = ld_stream(m4 + 2 * i + 1);
+                vq[u][0] = ld_stream(v4 + 2 * i);
+                vq[u][1] = ld_stream(v4 + 2 * i + 1);
+                if constexpr (sizeof(WT) == 2) {
+                    const uint4 h = ld_stream(reinterpret_cast<const uint4*>(w) + i);
+                    wq[u][0] = make_float4(h2f(lo16(h.x)), h2f(hi16(h.x)), h2f(lo16(h.y)),
+                                           h2f(hi16(h.y)));
+                    wq[u][1] = make_float4(h2f(lo16(h.z)), h2f(hi16(h.z)), h2f(lo16(h.w)),
+                                           h2f(hi16(h.w)));
+                } else {
+                    wq[u][0] = ld_stream(reinterpret_cast<const float4*>(w) + 2 * i);
+                    wq[u][1] = ld_stream(reinterpret_cast<const float4*>(w) + 2 * i + 1);
+                }
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const uint64_t i = base + u * stride;
+            if (i >= n8) continue;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                float4& ww = wq[u][h];
+                float4& mm = mq[u][h];
+                float4& vv = vq[u][h];
+                const float4 gg = gq[u][h];
+                ww.x = adam_elem(ww.x, gg.x, mm.x, vv.x, k, k.decay);
+                ww.y = adam_elem(ww.y, gg.y, mm.y, vv.y, k, k.decay);
+                ww.z = adam_elem(ww.z, gg.z, mm.z, vv.z, k, k.decay);
+                ww.w = adam_elem(ww.w, gg.w, mm.w, vv.w, k, k.decay);
+                st_stream(m4 + 2 * i + h, mm);
+                st_stream(v4 + 2 * i + h, vv);
+            }
+            if constexpr (sizeof(WT) == 2) {
+                uint4 o;
+                o.x = pack16(f2h(wq[u][0].x), f2h(wq[u][0].y));
+                o.y = pack16(f2h(wq[u][0].z), f2h(wq[u][0].w));
+                o.z = pack16(f2h(wq[u][1].x), f2h(wq[u][1].y));
+                o.w = pack16(f2h(wq[u][1].z), f2h(wq[u][1].w));
+                st_stream(reinterpret_cast<uint4*>(w) + i, o);
+            } else {
+                st_stream(reinterpret_cast<float4*>(w) + 2 * i, wq[u][0]);
+                st_stream(reinterpret_cast<float4*>(w) + 2 * i + 1, wq[u][1]);
+            }
+        }
+    }
+    // ragged tail (n % 8): the reference's scalar tail arithmetic
+    if (blockIdx.x == 0 && threadIdx.x < (a.n & 7u)) {
+        const uint64_t i = (n8 << 3) + threadIdx.x;
+        float mi = m[i], vi = v[i];
+        const float wn = adam_elem(WTraits<WT>::load(w, i), g[i], mi, vi, k, k.decay);
+        m[i] = mi;
+        v[i] = vi;
+        WTraits<WT>::store(w, i, wn);
+    }
+}
+
 // Scalar path for arbitrarily aligned pointers.
 template <typename WT>
 __global__ void __launch_bounds__(kT) adam_scalar_kernel(WT* w, const float* g, float* m, float* v,
@@ -207,13 +320,24 @@ static int adam_launch(WT* w, const float* g, float* m, float* v, uint64_t n, fl
     if (rc) return rc;
     AdamArgs a{n, lr, b1, b2, eps, wd, t};
     cudaStream_t s = legacy_stream(c);
-    const bool vec = aligned16(g) && aligned16(m) && aligned16(v) &&
-                     (sizeof(WT) == 2 ? ((reinterpret_cast<uintptr_t>(w) & 7u) == 0) : aligned16(w));
-    if (vec) {
-        const int blocks = streaming_grid(reinterpret_cast<const void*>(adam_vec_kernel<WT>), kT, 0,
-                                          (n >> 2) + 1);
-        adam_vec_kernel<WT><<<blocks, kT, 0, s>>>(w, g, m, v, a);
-    } else {
+    const bool gmv16 = aligned16(g) && aligned16(m) && aligned16(v);
+    bool launched = false;
+    if (gmv16 && aligned16(w)) {
+        constexpr int U = 2;
+        const int blocks = streaming_grid(reinterpret_cast<const void*>(adam_vec8_kernel<WT, U>),
+                                          kT, 0, (n >> 3) / U + 1);
+        adam_vec8_kernel<WT, U><<<blocks, kT, 0, s>>>(w, g, m, v, a);
+        launched = true;
+    }
+    if constexpr (sizeof(WT) == 2) {   // FP16 weights 8- but not 16-byte aligned
+        if (!launched && gmv16 && (reinterpret_cast<uintptr_t>(w) & 7u) == 0) {
+            const int blocks = streaming_grid(reinterpret_cast<const void*>(adam_vec_kernel<WT>),
+                                              kT, 0, (n >> 2) + 1);
+            adam_vec_kernel<WT><<<blocks, kT, 0, s>>>(w, g, m, v, a);
+            launched = true;
+        }
+    }
+    if (!launched) {
         const int blocks = streaming_grid(reinterpret_cast<const void*>(adam_scalar_kernel<WT>), kT,
                                           0, n);
         adam_scalar_kernel<WT><<<blocks, kT, 0, s>>>(w, g, m, v, a);
@@ -230,22 +354,36 @@ struct ClipScratch {
     ClipResult* res;
 };
 
+constexpr int kClipU = 4;   // float4 loads in flight per thread (norm and scale kernels)
+
 __global__ void __launch_bounds__(kT) clip_norm_kernel(const float* __restrict__ g, uint64_t n,
                                                       float thr, ClipScratch sc) {
     __shared__ double s_sum[kT / 32];
     __shared__ int s_last;
-    double acc = 0.0;
+    double acc = 0.0, acc1 = 0.0;
     const uint64_t stride = (uint64_t)gridDim.x * kT;
     if (aligned16(g)) {
+        // rounds of kClipU float4 loads per thread, all issued before any is
+        // squared; two accumulators halve the dependent chain of double FMAs
         const uint64_t nq = n >> 2;
         const float4* g4 = reinterpret_cast<const float4*>(g);
-        for (uint64_t i = (uint64_t)blockIdx.x * kT + threadIdx.x; i < nq; i += stride) {
-            const float4 x = __ldcg(g4 + i);
-            acc = __fma_rn((double)x.x, (double)x.x, acc);
-            acc = __fma_rn((double)x.y, (double)x.y, acc);
-            acc = __fma_rn((double)x.z, (double)x.z, acc);
-            acc = __fma_rn((double)x.w, (double)x.w, acc);
+        for (uint64_t base = (uint64_t)blockIdx.x * kT + threadIdx.x; base < nq;
+             base += stride * kClipU) {
+            float4 x[kClipU];
+#pragma unroll
+            for (int u = 0; u < kClipU; ++u) {
+                const uint64_t i = base + u * stride;
+                x[u] = i < nq ? __ldcg(g4 + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+#pragma unroll
+            for (int u = 0; u < kClipU; ++u) {
+                acc = __fma_rn((double)x[u].x, (double)x[u].x, acc);
+                acc1 = __fma_rn((double)x[u].y, (double)x[u].y, acc1);
+                acc = __fma_rn((double)x[u].z, (double)x[u].z, acc);
+                acc1 = __fma_rn((double)x[u].w, (double)x[u].w, acc1);
+            }
         }
+        acc += acc1;
         if (blockIdx.x == 0 && threadIdx.x < (n & 3u)) {
             const double x = g[(nq << 2) + threadIdx.x];
             acc = __fma_rn(x, x, acc);
@@ -304,13 +442,24 @@ __global__ void __launch_bounds__(kT) clip_scale_kernel(float* __restrict__ g, u
     if (aligned16(g)) {
         const uint64_t nq = n >> 2;
         float4* g4 = reinterpret_cast<float4*>(g);
-        for (uint64_t i = (uint64_t)blockIdx.x * kT + threadIdx.x; i < nq; i += stride) {
-            float4 x = ld_stream(g4 + i);
-            x.x = __fmul_rn(x.x, s);
-            x.y = __fmul_rn(x.y, s);
-            x.z = __fmul_rn(x.z, s);
-            x.w = __fmul_rn(x.w, s);
-            st_stream(g4 + i, x);
+        for (uint64_t base = (uint64_t)blockIdx.x * kT + threadIdx.x; base < nq;
+             base += stride * kClipU) {
+            float4 x[kClipU];
+#pragma unroll
+            for (int u = 0; u < kClipU; ++u) {
+                const uint64_t i = base + u * stride;
+                if (i < nq) x[u] = ld_stream(g4 + i);
+            }
+#pragma unroll
+            for (int u = 0; u < kClipU; ++u) {
+                const uint64_t i = base + u * stride;
+                if (i >= nq) continue;
+                x[u].x = __fmul_rn(x[u].x, s);
+                x[u].y = __fmul_rn(x[u].y, s);
+                x[u].z = __fmul_rn(x[u].z, s);
+                x[u].w = __fmul_rn(x[u].w, s);
+                st_stream(g4 + i, x[u]);
+            }
         }
         if (blockIdx.x == 0 && threadIdx.x < (n & 3u)) {
             const uint64_t i = (nq << 2) + threadIdx.x;
@@ -320,6 +469,16 @@ __global__ void __launch_bounds__(kT) clip_scale_kernel(float* __restrict__ g, u
         for (uint64_t i = (uint64_t)blockIdx.x * kT + threadIdx.x; i < n; i += stride)
             g[i] = __fmul_rn(g[i], s);
     }
+}
+
+// Grids of the two clip kernels (norm, scale) for n elements: one
+// definition for the allocating and the allocation-free entry points, whose
+// norms must agree bit for bit (the double sum's order depends on the grid).
+static void clip_grids(uint64_t n, int* norm_blocks, int* scale_blocks) {
+    *norm_blocks = streaming_grid(reinterpret_cast<const void*>(clip_norm_kernel), kT, 0,
+                                  (n >> 2) / kClipU + 1);
+    *scale_blocks = streaming_grid(reinterpret_cast<const void*>(clip_scale_kernel), kT, 0,
+                                   (n >> 2) / kClipU + 1);
 }
 
 static int clip_scratch(LegacyCtx* c, int blocks, ClipScratch* sc) {
@@ -350,8 +509,8 @@ static int clip_launch(float* g, uint64_t n, float thr, float* norm_out) {
     int rc = current_ctx(&c);
     if (rc) return rc;
     cudaStream_t s = legacy_stream(c);
-    const int blocks = streaming_grid(reinterpret_cast<const void*>(clip_norm_kernel), kT, 0,
-                                      (n >> 2) + 1);
+    int blocks = 0, sblocks = 0;
+    clip_grids(n, &blocks, &sblocks);
     ClipScratch sc;
     rc = clip_scratch(c, blocks, &sc);
     if (rc) return rc;
@@ -359,8 +518,6 @@ static int clip_launch(float* g, uint64_t n, float thr, float* norm_out) {
         clip_neon_fold_kernel<<<1, 32, 0, s>>>(g, n, thr, sc.res);
     else
         clip_norm_kernel<<<blocks, kT, 0, s>>>(g, n, thr, sc);
-    const int sblocks = streaming_grid(reinterpret_cast<const void*>(clip_scale_kernel), kT, 0,
-                                       (n >> 2) + 1);
     clip_scale_kernel<<<sblocks, kT, 0, s>>>(g, n, sc.res);
     if (cudaGetLastError() != cudaSuccess) return ARK_E_CUDA;
     ClipResult r;
@@ -416,20 +573,24 @@ static int clip_noalloc_launch(float* g, uint64_t n, float thr, float* norm_dev,
     if (rc) return rc;
     if (n == 0)   // empty: norm 0, nothing to scale (as ark_asm_grad_clip)
         return cudaMemsetAsync(norm_dev, 0, sizeof(float), s) == cudaSuccess ? ARK_OK : ARK_E_CUDA;
-    // the same grid as ark_asm_grad_clip, so both reduce in the same order
-    const int blocks = streaming_grid(reinterpret_cast<const void*>(clip_norm_kernel), kT, 0,
-                                      (n >> 2) + 1);
-    if (blocks > kNoAllocMaxBlocks) {
-        fprintf(stderr,
-                "[ark_cuda] ark_cuda_grad_clip_noalloc: needs %d block partials, the static "
-                "scratch holds %d\n", blocks, kNoAllocMaxBlocks);
-        return ARK_E_UNSUPPORTED;
+    // the same grids and kernels as ark_asm_grad_clip (the compat flag
+    // included), so both give the same norm bit for bit
+    int blocks = 0, sblocks = 0;
+    clip_grids(n, &blocks, &sblocks);
+    if (g_compat.load() & ARK_COMPAT_CLIP_NEON_FOLD) {
+        clip_neon_fold_kernel<<<1, 32, 0, s>>>(g, n, thr, sc.res);   // no block partials
+    } else {
+        if (blocks > kNoAllocMaxBlocks) {
+            fprintf(stderr,
+                    "[ark_cuda] ark_cuda_grad_clip_noalloc: needs %d block partials, the static "
+                    "scratch holds %d\n", blocks, kNoAllocMaxBlocks);
+            return ARK_E_UNSUPPORTED;
+        }
+        // the ticket must start at zero; a call that stopped early could have left it set
+        if (cudaMemsetAsync(sc.ticket, 0, sizeof(unsigned int), s) != cudaSuccess)
+            return ARK_E_CUDA;
+        clip_norm_kernel<<<blocks, kT, 0, s>>>(g, n, thr, sc);
     }
-    // the ticket must start at zero; a call that stopped early could have left it set
-    if (cudaMemsetAsync(sc.ticket, 0, sizeof(unsigned int), s) != cudaSuccess) return ARK_E_CUDA;
-    clip_norm_kernel<<<blocks, kT, 0, s>>>(g, n, thr, sc);
-    const int sblocks = streaming_grid(reinterpret_cast<const void*>(clip_scale_kernel), kT, 0,
-                                       (n >> 2) + 1);
     clip_scale_kernel<<<sblocks, kT, 0, s>>>(g, n, sc.res);
     if (cudaGetLastError() != cudaSuccess) return ARK_E_CUDA;
     if (cudaMemcpyAsync(norm_dev, &sc.res->norm, sizeof(float), cudaMemcpyDeviceToDevice, s) !=
@@ -439,6 +600,7 @@ static int clip_noalloc_launch(float* g, uint64_t n, float thr, float* norm_dev,
 }
 
 // ------------------------------------------------------------ conversions
+constexpr int kConvU = 2;   // 8-element vectors in flight per thread
 __global__ void __launch_bounds__(kT) quant_kernel(const float* __restrict__ src,
                                                   uint16_t* __restrict__ dst, uint64_t n, int vec) {
     const uint64_t stride = (uint64_t)gridDim.x * kT;
@@ -447,14 +609,28 @@ __global__ void __launch_bounds__(kT) quant_kernel(const float* __restrict__ src
         const uint64_t n8 = n >> 3;
         const float4* s4 = reinterpret_cast<const float4*>(src);
         uint4* d4 = reinterpret_cast<uint4*>(dst);
-        for (uint64_t i = (uint64_t)blockIdx.x * kT + threadIdx.x; i < n8; i += stride) {
-            const float4 a = ld_stream(s4 + 2 * i), b = ld_stream(s4 + 2 * i + 1);
-            uint4 o;
-            o.x = pack16(f2h(a.x), f2h(a.y));
-            o.y = pack16(f2h(a.z), f2h(a.w));
-            o.z = pack16(f2h(b.x), f2h(b.y));
-            o.w = pack16(f2h(b.z), f2h(b.w));
-            st_stream(d4 + i, o);
+        for (uint64_t base = (uint64_t)blockIdx.x * kT + threadIdx.x; base < n8;
+             base += stride * kConvU) {
+            float4 a[kConvU], b[kConvU];
+#pragma unroll
+            for (int u = 0; u < kConvU; ++u) {
+                const uint64_t i = base + u * stride;
+                if (i < n8) {
+                    a[u] = ld_stream(s4 + 2 * i);
+                    b[u] = ld_stream(s4 + 2 * i + 1);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < kConvU; ++u) {
+                const uint64_t i = base + u * stride;
+                if (i >= n8) continue;
+                uint4 o;
+                o.x = pack16(f2h(a[u].x), f2h(a[u].y));
+                o.y = pack16(f2h(a[u].z), f2h(a[u].w));
+                o.z = pack16(f2h(b[u].x), f2h(b[u].y));
+                o.w = pack16(f2h(b[u].z), f2h(b[u].w));
+                st_stream(d4 + i, o);
+            }
         }
         done = n8 << 3;
     }
@@ -470,12 +646,23 @@ __global__ void __launch_bounds__(kT) dequant_kernel(const uint16_t* __restrict_
         const uint64_t n8 = n >> 3;
         const uint4* s4 = reinterpret_cast<const uint4*>(src);
         float4* d4 = reinterpret_cast<float4*>(dst);
-        for (uint64_t i = (uint64_t)blockIdx.x * kT + threadIdx.x; i < n8; i += stride) {
-            const uint4 q = ld_stream(s4 + i);
-            st_stream(d4 + 2 * i, make_float4(h2f(lo16(q.x)), h2f(hi16(q.x)), h2f(lo16(q.y)),
-                                              h2f(hi16(q.y))));
-            st_stream(d4 + 2 * i + 1, make_float4(h2f(lo16(q.z)), h2f(hi16(q.z)),
-                                                  h2f(lo16(q.w)), h2f(hi16(q.w))));
+        for (uint64_t base = (uint64_t)blockIdx.x * kT + threadIdx.x; base < n8;
+             base += stride * kConvU) {
+            uint4 q[kConvU];
+#pragma unroll
+            for (int u = 0; u < kConvU; ++u) {
+                const uint64_t i = base + u * stride;
+                if (i < n8) q[u] = ld_stream(s4 + i);
+            }
+#pragma unroll
+            for (int u = 0; u < kConvU; ++u) {
+                const uint64_t i = base + u * stride;
+                if (i >= n8) continue;
+                st_stream(d4 + 2 * i, make_float4(h2f(lo16(q[u].x)), h2f(hi16(q[u].x)),
+                                                  h2f(lo16(q[u].y)), h2f(hi16(q[u].y))));
+                st_stream(d4 + 2 * i + 1, make_float4(h2f(lo16(q[u].z)), h2f(hi16(q[u].z)),
+                                                      h2f(lo16(q[u].w)), h2f(hi16(q[u].w))));
+            }
         }
         done = n8 << 3;
     }
@@ -493,12 +680,12 @@ static int convert_launch(const void* src, void* dst, uint64_t n, bool quant) {
     cudaStream_t s = legacy_stream(c);
     if (quant) {
         const int blocks = streaming_grid(reinterpret_cast<const void*>(quant_kernel), kT, 0,
-                                          vec ? (n >> 3) + 1 : n);
+                                          vec ? (n >> 3) / kConvU + 1 : n);
         quant_kernel<<<blocks, kT, 0, s>>>(static_cast<const float*>(src),
                                             static_cast<uint16_t*>(dst), n, vec);
     } else {
         const int blocks = streaming_grid(reinterpret_cast<const void*>(dequant_kernel), kT, 0,
-                                          vec ? (n >> 3) + 1 : n);
+                                          vec ? (n >> 3) / kConvU + 1 : n);
         dequant_kernel<<<blocks, kT, 0, s>>>(static_cast<const uint16_t*>(src),
                                               static_cast<float*>(dst), n, vec);
     }

@@ -47,6 +47,9 @@ struct Partial {
 };
 constexpr unsigned long long kPartialTimeout = ~0ull;
 constexpr int kMaxP2PRanks = 32;
+constexpr int kSlotWords = 8;
+enum SlotWord { kSlotSum = 0, kSlotBad = 1, kSlotEpoch = 2, kSlotGradsReady = 3,
+                kSlotWeightsReady = 4 };
 
 struct StepParams {
     const uint16_t* g16;
@@ -69,13 +72,20 @@ struct StepParams {
     unsigned int* ticket2;
     Partial* part_local;             // this rank's partial (NCCL all-gather send buffer)
     Partial* part_all;               // [world] partials of every rank, rank order
-    uint64_t* xchg;                  // own receive slots [2][world] x {sum, bad, epoch, pad}
+    uint64_t* xchg;                  // own receive slots [2][world] x kSlotWords (slot_of)
     uint64_t* const* peers;          // every rank's receive slots (peers[rank] == xchg)
     uint64_t peer_timeout_ns;
+    unsigned long long* verdict;     // pass 2: (epoch << 1) | every partial arrived
+    unsigned long long* logits_bad;  // non-finite logits gradients counted since the last step
     // reduce-scatter step: every rank's full FP16 gradient buffer (mapped here)
     const uint16_t* const* gsrc;
     uint16_t* g16_out;               // this rank's reduced shard
     float* w32_out;                  // optional FP32 copy of the updated weights
+    // weight all-gather fused with pass 2: every rank's full FP16 weight
+    // buffer (mapped here); the updated shard is stored into each of them,
+    // into this rank's own too when wself (w16 is not that buffer's slice)
+    uint16_t* const* wdst;           // [world], device memory
+    int wself;
 };
 
 constexpr int kThreads = 256;
@@ -142,47 +152,87 @@ __device__ __forceinline__ void accum8_pow2(uint4 q, uint64_t gi0, uint64_t keep
     }
 }
 
-// Receive slot of rank q in rank r's buffer, for one epoch parity: 4 x u64
-// {sum of squares, non-finite, partial epoch, gradients-ready epoch}.
+// Receive slot of rank q in rank r's buffer, for one epoch parity:
+// kSlotWords x u64 {sum of squares, non-finite, partial epoch,
+// gradients-ready epoch, weights-ready epoch, unused...} (one 64-byte line).
 __device__ __forceinline__ uint64_t* slot_of(uint64_t* base, unsigned long long epoch, int world,
                                              int q) {
-    return base + (((epoch & 1ull) * (unsigned long long)world + (unsigned long long)q) * 4);
+    return base + (((epoch & 1ull) * (unsigned long long)world + (unsigned long long)q) *
+                   kSlotWords);
 }
 
 // Last pass-1 block, world > 1 over mapped peer slots: lane r (< world) of
 // warp 0 stores this rank's partial into rank r's slot [epoch & 1][rank]
-// (payload, then the epoch with release semantics) and waits, bounded by
-// the global timer, for rank r's partial in this rank's slot
-// [epoch & 1][r].  Slots alternate with the epoch parity, so a rank that
-// runs one step ahead never overwrites a partial its peer has not read.
-__device__ void exchange_p2p(const StepParams& p, double my_sum, unsigned long long my_bad) {
+// (payload, then the epoch with release semantics) and returns: pass 1
+// never waits for a peer.  The wait is in pass 2 (gather_partials_p2p),
+// where it overlaps the first round of loads.  Slots alternate with the
+// epoch parity: a rank publishes epoch e + 2 into the slot of epoch e only
+// after its pass 2 of step e + 1 has seen every rank's partial e + 1, which
+// every rank publishes only after its own pass 2 of step e (the last reader
+// of epoch e) has completed.
+__device__ void publish_partial_p2p(const StepParams& p, double my_sum,
+                                    unsigned long long my_bad) {
     const int r = threadIdx.x;
     if (r >= p.world) return;
     const unsigned long long epoch = p.st->steps_called + 1ull;
     uint64_t* dst = slot_of(p.peers[r], epoch, p.world, p.rank);
-    st_relaxed_sys_v2(dst, (uint64_t)__double_as_longlong(my_sum), my_bad);
-    st_release_sys(dst + 2, epoch);
-    const uint64_t* src = slot_of(p.xchg, epoch, p.world, r);
+    st_relaxed_sys_v2(dst + kSlotSum, (uint64_t)__double_as_longlong(my_sum), my_bad);
+    st_release_sys(dst + kSlotEpoch, epoch);
+}
+
+// Bounded wait of one lane for rank q's partial of `epoch` in this rank's
+// slots.  Returns false if it did not arrive within the limit.
+__device__ bool wait_partial(const StepParams& p, unsigned long long epoch, int q, Partial* out) {
+    const uint64_t* src = slot_of(p.xchg, epoch, p.world, q);
     const uint64_t t0 = global_ns();
-    bool ok = true;
-    while (ld_acquire_sys(src + 2) != epoch) {
-        if (global_ns() - t0 > p.peer_timeout_ns) {
-            ok = false;
-            break;
-        }
+    while (ld_acquire_sys(src + kSlotEpoch) != epoch) {
+        if (global_ns() - t0 > p.peer_timeout_ns) return false;
         __nanosleep(32);
     }
-    Partial got;
-    if (ok) {
-        uint64_t x, y;
-        ld_relaxed_sys_v2(src, x, y);
-        got.sumsq = __longlong_as_double((long long)x);
-        got.nonfinite = y;
-    } else {
-        got.sumsq = 0.0;
-        got.nonfinite = kPartialTimeout;
+    uint64_t x, y;
+    ld_relaxed_sys_v2(src + kSlotSum, x, y);
+    out->sumsq = __longlong_as_double((long long)x);
+    out->nonfinite = y;
+    return true;
+}
+
+// Pass 2, every block, warp 0: this step's partial of every rank from this
+// rank's receive slots into out[0, world) (shared memory).  The outcome is
+// made uniform across the grid's blocks: the first block to decide (every
+// partial arrived, or a wait ran out) records (epoch << 1 | ok) in
+// p.verdict with a compare-and-swap and every block follows it, so no block
+// updates while another skips.  A block that timed out while the verdict
+// says every partial arrived reads them again (they are in this GPU's
+// memory by then); if even that wait runs out it marks its partials as
+// missing (its vectors are not updated) and the state reports
+// ARK_E_TIMEOUT.  Returns in lane 0 of warp 0.
+__device__ void gather_partials_p2p(const StepParams& p, Partial* out) {
+    const int lane = threadIdx.x;
+    const unsigned long long epoch = p.st->steps_called + 1ull;
+    bool ok = true;
+    if (lane < p.world) ok = wait_partial(p, epoch, lane, &out[lane]);
+    const bool all_ok = __all_sync(0xFFFFFFFFu, ok);
+    unsigned long long v = 0;
+    if (lane == 0) {
+        const unsigned long long mine = (epoch << 1) | (all_ok ? 1ull : 0ull);
+        v = *reinterpret_cast<volatile unsigned long long*>(p.verdict);
+        while ((v >> 1) != epoch) {
+            const unsigned long long w = atomicCAS(p.verdict, v, mine);
+            if (w == v) {
+                v = mine;
+                break;
+            }
+            v = w;
+        }
     }
-    p.part_all[r] = got;
+    v = __shfl_sync(0xFFFFFFFFu, v, 0);
+    const bool verdict_ok = (v & 1ull) != 0;
+    if (verdict_ok && !all_ok && lane < p.world && !ok) ok = wait_partial(p, epoch, lane, &out[lane]);
+    if (lane < p.world && (!verdict_ok || !ok)) {
+        out[lane].sumsq = 0.0;
+        out[lane].nonfinite = kPartialTimeout;
+    }
+    __syncwarp();
 }
 
 // Per-thread pass-1 accumulators.
@@ -224,14 +274,6 @@ __device__ __forceinline__ void p1_consume(P1Acc& a, const uint4 q, uint64_t vec
         a.amax = absmax2(a.amax, q.w);
         accum8_general(q, gi0, sc.inv, p.keep_lo, p.keep_hi, a.acc0, a.acc1);
     }
-}
-
-// Either path, chosen per step by the loss scale (uniform across the grid).
-template <bool KEEP>
-__device__ __forceinline__ void p1_consume_any(P1Acc& a, const uint4 q, uint64_t vec,
-                                               const P1Scale& sc, const StepParams& p) {
-    if (sc.pow2) p1_consume<KEEP, true>(a, q, vec, sc, p);
-    else p1_consume<KEEP, false>(a, q, vec, sc, p);
 }
 
 __device__ __forceinline__ void p1_consume1(P1Acc& a, uint16_t h, uint64_t i, const P1Scale& sc,
@@ -284,13 +326,22 @@ __device__ void p1_finish(const P1Acc& a, const P1Scale& sc, bool failed, const 
     b = block_sum_u64<kThreads>(b, s_bad);
     f = block_sum_u64<kThreads>(f, s_bad);
     if (f) b = kPartialTimeout;
+    // Non-finite logits gradients counted by the logits check since the last
+    // step (training.rs:228-241) skip this step like non-finite gradients:
+    // the reference applies the same transitions on both paths (:232-236,
+    // :294-298).  Folding the count into the rank partial makes every rank
+    // skip when any rank's logits were non-finite.
+    if (threadIdx.x == 0) {
+        const unsigned long long lb = atomicExch(p.logits_bad, 0ull);
+        if (b != kPartialTimeout) b += lb;
+    }
     if (p.p2p) {
         if (threadIdx.x == 0) {
             s_sum[0] = s;
             s_bad[0] = b;
         }
         __syncthreads();
-        if (threadIdx.x < kMaxP2PRanks) exchange_p2p(p, s_sum[0], s_bad[0]);
+        if (threadIdx.x < kMaxP2PRanks) publish_partial_p2p(p, s_sum[0], s_bad[0]);
     } else if (threadIdx.x == 0) {
         p.part_local->sumsq = s;
         p.part_local->nonfinite = b;   // threads that saw an inf/NaN (> 0 iff any)
@@ -374,12 +425,13 @@ __device__ bool reduce_ready_barrier(const StepParams& p) {
     if (p.world > 1) {
         if (blockIdx.x == 0 && threadIdx.x < p.world) {
             __threadfence_system();
-            st_release_sys(slot_of(p.peers[threadIdx.x], epoch, p.world, p.rank) + 3, epoch);
+            st_release_sys(slot_of(p.peers[threadIdx.x], epoch, p.world, p.rank) + kSlotGradsReady,
+                           epoch);
         }
         if (threadIdx.x == 0) {
             const uint64_t t0 = global_ns();
             for (int q = 0; q < p.world && !s_fail; ++q) {
-                const uint64_t* ready = slot_of(p.xchg, epoch, p.world, q) + 3;
+                const uint64_t* ready = slot_of(p.xchg, epoch, p.world, q) + kSlotGradsReady;
                 while (ld_acquire_sys(ready) != epoch) {
                     if (global_ns() - t0 > p.peer_timeout_ns) {
                         s_fail = 1;
@@ -394,61 +446,75 @@ __device__ bool reduce_ready_barrier(const StepParams& p) {
     return s_fail != 0;
 }
 
-template <int U, int MINB>
+// Any rank count: U vectors of every rank per round, rank by rank.
+template <int U, bool KEEP, bool POW2>
+__device__ __forceinline__ void reduce_stream(P1Acc& a, const P1Scale& sc, const StepParams& p) {
+    const uint64_t nvec = p.n >> 3;
+    const uint64_t stride = (uint64_t)gridDim.x * kThreads;
+    uint4* out = reinterpret_cast<uint4*>(p.g16_out);
+    for (uint64_t base = (uint64_t)blockIdx.x * kThreads + threadIdx.x; base < nvec;
+         base += stride * U) {
+        float acc[U][8];
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc[u][j] = 0.0f;
+        for (int r = 0; r < p.world; ++r) {                 // rank order
+            const uint4* src = reinterpret_cast<const uint4*>(p.gsrc[r] + p.offset);
+            uint4 q[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const uint64_t i = base + u * stride;
+                q[u] = i < nvec ? __ldcg(src + i) : make_uint4(0, 0, 0, 0);
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                const uint32_t w[4] = {q[u].x, q[u].y, q[u].z, q[u].w};
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                    acc[u][j] = __fadd_rn(acc[u][j],
+                                          h2f((j & 1) ? hi16(w[j >> 1]) : lo16(w[j >> 1])));
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const uint64_t i = base + u * stride;
+            if (i < nvec) {
+                uint32_t w[4];
+#pragma unroll
+                for (int k = 0; k < 4; ++k) w[k] = pack16(f2h(acc[u][2 * k]), f2h(acc[u][2 * k + 1]));
+                const uint4 rq = make_uint4(w[0], w[1], w[2], w[3]);
+                out[i] = rq;
+                p1_consume<KEEP, POW2>(a, rq, i, sc, p);
+            }
+        }
+    }
+}
+
+// Ragged tail (n % 8) of the reduce-scatter step, block 0.
+__device__ __forceinline__ void reduce_tail(P1Acc& a, const P1Scale& sc, const StepParams& p) {
+    if (blockIdx.x == 0 && threadIdx.x < (p.n & 7u)) {
+        const uint64_t i = (p.n & ~7ull) + threadIdx.x;
+        float f = 0.0f;
+        for (int r = 0; r < p.world; ++r) f = __fadd_rn(f, h2f(p.gsrc[r][p.offset + i]));
+        const uint16_t h = f2h(f);
+        p.g16_out[i] = h;
+        p1_consume1(a, h, i, sc, p);
+    }
+}
+
+// KEEP: the compat kept range is non-empty (chosen on the host); the
+// power-of-two path is chosen per step by the loss scale, as in pass 1.
+template <int U, int MINB, bool KEEP>
 __global__ void __launch_bounds__(kThreads, MINB) pass1_reduce_kernel(StepParams p) {
     griddep_launch_dependents();
     const bool failed = reduce_ready_barrier(p);
     const P1Scale sc = p1_scale(p);
     P1Acc a;
-    const uint64_t nvec = p.n >> 3;
-    const uint64_t stride = (uint64_t)gridDim.x * kThreads;
-    uint4* out = reinterpret_cast<uint4*>(p.g16_out);
     if (!failed) {
-        for (uint64_t base = (uint64_t)blockIdx.x * kThreads + threadIdx.x; base < nvec;
-             base += stride * U) {
-            float acc[U][8];
-#pragma unroll
-            for (int u = 0; u < U; ++u)
-#pragma unroll
-                for (int j = 0; j < 8; ++j) acc[u][j] = 0.0f;
-            for (int r = 0; r < p.world; ++r) {                 // rank order
-                const uint4* src = reinterpret_cast<const uint4*>(p.gsrc[r] + p.offset);
-                uint4 q[U];
-#pragma unroll
-                for (int u = 0; u < U; ++u) {
-                    const uint64_t i = base + u * stride;
-                    q[u] = i < nvec ? __ldcg(src + i) : make_uint4(0, 0, 0, 0);
-                }
-#pragma unroll
-                for (int u = 0; u < U; ++u) {
-                    const uint32_t w[4] = {q[u].x, q[u].y, q[u].z, q[u].w};
-#pragma unroll
-                    for (int j = 0; j < 8; ++j)
-                        acc[u][j] = __fadd_rn(acc[u][j],
-                                              h2f((j & 1) ? hi16(w[j >> 1]) : lo16(w[j >> 1])));
-                }
-            }
-#pragma unroll
-            for (int u = 0; u < U; ++u) {
-                const uint64_t i = base + u * stride;
-                if (i < nvec) {
-                    uint32_t w[4];
-#pragma unroll
-                    for (int k = 0; k < 4; ++k) w[k] = pack16(f2h(acc[u][2 * k]), f2h(acc[u][2 * k + 1]));
-                    const uint4 rq = make_uint4(w[0], w[1], w[2], w[3]);
-                    out[i] = rq;
-                    p1_consume_any<true>(a, rq, i, sc, p);
-                }
-            }
-        }
-        if (blockIdx.x == 0 && threadIdx.x < (p.n & 7u)) {   // ragged tail (n % 8)
-            const uint64_t i = (nvec << 3) + threadIdx.x;
-            float f = 0.0f;
-            for (int r = 0; r < p.world; ++r) f = __fadd_rn(f, h2f(p.gsrc[r][p.offset + i]));
-            const uint16_t h = f2h(f);
-            p.g16_out[i] = h;
-            p1_consume1(a, h, i, sc, p);
-        }
+        if (sc.pow2) reduce_stream<U, KEEP, true>(a, sc, p);
+        else reduce_stream<U, KEEP, false>(a, sc, p);
+        reduce_tail(a, sc, p);
     }
     p1_finish(a, sc, failed, p);
 }
@@ -464,6 +530,7 @@ struct Plan {
     int clip;
     int overflow;
     int error;      // ARK_E_* raised while forming the plan (0 = none)
+    unsigned long long epoch;   // this step's number (steps_called + 1)
 };
 
 // The step plan, in two parts.  plan_from_state reads only the state (last
@@ -472,6 +539,7 @@ struct Plan {
 // every rank's {sum, non-finite}, which pass 1 writes.
 __device__ void plan_from_state(const StepParams& p, Plan& pl) {
     const ark_opt_status st = *p.st;
+    pl.epoch = st.steps_called + 1ull;
     pl.early_stop = st.early_stop != 0;
     pl.inv = __fdiv_rn(1.0f, st.loss_scale);          // training.rs:244
     pl.t = st.opt_step + 1u;                          // optimizer.rs:172
@@ -480,12 +548,12 @@ __device__ void plan_from_state(const StepParams& p, Plan& pl) {
     pl.k = adam_scalars(pl.lr, p.beta1, p.beta2, p.eps, p.wd, pl.t);
 }
 
-__device__ void plan_from_partials(const StepParams& p, Plan& pl) {
+__device__ void plan_from_partials(const StepParams& p, const Partial* parts, Plan& pl) {
     double sumsq = 0.0;
     unsigned long long bad = 0;
     bool timeout = false;
     for (int r = 0; r < p.world; ++r) {               // rank order: deterministic
-        const Partial q = p.part_all[r];
+        const Partial q = parts[r];
         if (q.nonfinite == kPartialTimeout) timeout = true;
         else {
             sumsq += q.sumsq;
@@ -613,7 +681,7 @@ __device__ __forceinline__ void p2_load_g(P2Round<U>& r, uint64_t base, uint64_t
     }
 }
 
-template <int U, bool kW32, bool KEEP, int DEC>
+template <int U, bool kW32, bool KEEP, int DEC, bool GATHER>
 __device__ __forceinline__ void p2_update(P2Round<U>& r, uint64_t base, uint64_t stride,
                                           uint64_t nvec, uint4* w4, float4* m4, float4* v4,
                                           const Plan& pl, const StepParams& p) {
@@ -625,6 +693,12 @@ __device__ __forceinline__ void p2_update(P2Round<U>& r, uint64_t base, uint64_t
             update8<KEEP, DEC>(r.wq[u], r.gq[u], r.ma[u], r.mb[u], r.va[u], r.vb[u],
                           p.offset + (i << 3), pl, p);
             st_stream(w4 + i, r.wq[u]);
+            if (GATHER) {   // every rank's full weight buffer: plain (peer) stores
+                const uint64_t gv = (p.offset >> 3) + i;
+                for (int q = 0; q < p.world; ++q)
+                    if (q != p.rank || p.wself)
+                        reinterpret_cast<uint4*>(p.wdst[q])[gv] = r.wq[u];
+            }
             if (kW32) {   // the forward's FP32 weights (training.rs:165-186)
                 float4* o = reinterpret_cast<float4*>(p.w32_out) + 2 * i;
                 const uint4 wq = r.wq[u];
@@ -648,13 +722,14 @@ __device__ __forceinline__ void p2_update(P2Round<U>& r, uint64_t base, uint64_t
 // 1's retire: before griddep_wait they form the state part of the plan and
 // load their first round of w, m, v (and g, unless pass 1 writes it: the
 // reduce-scatter step), none of which pass 1 writes.
-template <int kUnroll2, int MINB, bool kW32, bool KEEP, int DEC = 1>
+template <int kUnroll2, int MINB, bool kW32, bool KEEP, int DEC = 1, bool GATHER = false>
 __global__ void __launch_bounds__(kThreads, MINB) pass2_kernel(StepParams p,
                                                               uint16_t* __restrict__ w16,
                                                               float* __restrict__ m,
                                                               float* __restrict__ v) {
     __shared__ Plan s_plan;
     __shared__ int s_last;
+    __shared__ Partial s_part[kMaxP2PRanks];
     const uint4* g4 = reinterpret_cast<const uint4*>(p.g16);
     uint4* w4 = reinterpret_cast<uint4*>(w16);
     float4* m4 = reinterpret_cast<float4*>(m);
@@ -667,13 +742,23 @@ __global__ void __launch_bounds__(kThreads, MINB) pass2_kernel(StepParams p,
     P2Round<kUnroll2> r;
     p2_load<kUnroll2>(r, base, stride, nvec, g4, w4, m4, v4, g_early);
     griddep_wait();
-    if (threadIdx.x == 0) plan_from_partials(p, s_plan);
+    if (p.p2p) {   // every rank's partial, from this rank's receive slots (bounded wait)
+        if (threadIdx.x < 32) gather_partials_p2p(p, s_part);
+        if (threadIdx.x == 0) {
+            plan_from_partials(p, s_part, s_plan);
+            // a block that could not read a partial reports it (the last
+            // block folds it into the state); see gather_partials_p2p
+            if (s_plan.error) atomicExch(&p.st->error, s_plan.error);
+        }
+    } else if (threadIdx.x == 0) {
+        plan_from_partials(p, p.part_all, s_plan);
+    }
     __syncthreads();
     const Plan pl = s_plan;
     if (!pl.skip) {
         if (!g_early) p2_load_g<kUnroll2>(r, base, stride, nvec, g4);
         while (base < nvec) {
-            p2_update<kUnroll2, kW32, KEEP, DEC>(r, base, stride, nvec, w4, m4, v4, pl, p);
+            p2_update<kUnroll2, kW32, KEEP, DEC, GATHER>(r, base, stride, nvec, w4, m4, v4, pl, p);
             base += stride * kUnroll2;
             if (base >= nvec) break;
             p2_load<kUnroll2>(r, base, stride, nvec, g4, w4, m4, v4, true);
@@ -686,73 +771,168 @@ __global__ void __launch_bounds__(kThreads, MINB) pass2_kernel(StepParams p,
             if (pl.clip) gf = __fmul_rn(gf, pl.s);
             const float decay = gi < p.n_decay ? pl.k.decay : 1.0f;
             float mi = m[i], vi = v[i];
-            w16[i] = f2h(adam_elem(h2f(w16[i]), gf, mi, vi, pl.k, decay));
-            if (kW32) p.w32_out[i] = h2f(w16[i]);
+            const uint16_t wn = f2h(adam_elem(h2f(w16[i]), gf, mi, vi, pl.k, decay));
+            w16[i] = wn;
+            if (kW32) p.w32_out[i] = h2f(wn);
+            if (GATHER)
+                for (int q = 0; q < p.world; ++q)
+                    if (q != p.rank || p.wself) p.wdst[q][gi] = wn;
             m[i] = mi;
             v[i] = vi;
         }
     }
+    // peer stores of this block visible system-wide before it is counted
+    if (GATHER) __threadfence_system();
     if (!last_block_arrived(p.ticket2, &s_last)) return;
     if (threadIdx.x == 0) advance_state(p, pl);
+    if (GATHER && p.p2p && threadIdx.x < p.world) {
+        // weights-ready epoch into every rank's slot: every block's stores
+        // into that rank's weight buffer precede it
+        __threadfence_system();
+        st_release_sys(slot_of(p.peers[threadIdx.x], pl.epoch, p.world, p.rank) +
+                           kSlotWeightsReady,
+                       pl.epoch);
+    }
 }
 
 // The same for a fixed rank count NR: all NR x U loads of a thread are in
 // flight before any addition (remote loads over NVLink have long latency).
-template <int NR, int U, int MINB>
-__global__ void __launch_bounds__(kThreads, MINB) pass1_reduce_nr_kernel(StepParams p) {
-    griddep_launch_dependents();
-    const bool failed = reduce_ready_barrier(p);
-    const P1Scale sc = p1_scale(p);
-    P1Acc a;
+template <int NR, int U, bool KEEP, bool POW2>
+__device__ __forceinline__ void reduce_stream_nr(P1Acc& a, const P1Scale& sc,
+                                                 const StepParams& p) {
     const uint64_t nvec = p.n >> 3;
     const uint64_t stride = (uint64_t)gridDim.x * kThreads;
     uint4* out = reinterpret_cast<uint4*>(p.g16_out);
     const uint4* src[NR];
 #pragma unroll
     for (int r = 0; r < NR; ++r) src[r] = reinterpret_cast<const uint4*>(p.gsrc[r] + p.offset);
-    if (!failed) {
-        for (uint64_t base = (uint64_t)blockIdx.x * kThreads + threadIdx.x; base < nvec;
-             base += stride * U) {
-            uint4 q[NR][U];
+    for (uint64_t base = (uint64_t)blockIdx.x * kThreads + threadIdx.x; base < nvec;
+         base += stride * U) {
+        uint4 q[NR][U];
 #pragma unroll
-            for (int r = 0; r < NR; ++r)
-#pragma unroll
-                for (int u = 0; u < U; ++u) {
-                    const uint64_t i = base + u * stride;
-                    q[r][u] = i < nvec ? __ldcg(src[r] + i) : make_uint4(0, 0, 0, 0);
-                }
+        for (int r = 0; r < NR; ++r)
 #pragma unroll
             for (int u = 0; u < U; ++u) {
                 const uint64_t i = base + u * stride;
-                if (i >= nvec) continue;
-                float acc[8];
-#pragma unroll
-                for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
-#pragma unroll
-                for (int r = 0; r < NR; ++r) {                 // rank order
-                    const uint32_t w[4] = {q[r][u].x, q[r][u].y, q[r][u].z, q[r][u].w};
-#pragma unroll
-                    for (int j = 0; j < 8; ++j)
-                        acc[j] = __fadd_rn(acc[j], h2f((j & 1) ? hi16(w[j >> 1]) : lo16(w[j >> 1])));
-                }
-                uint32_t w[4];
-#pragma unroll
-                for (int k = 0; k < 4; ++k) w[k] = pack16(f2h(acc[2 * k]), f2h(acc[2 * k + 1]));
-                const uint4 rq = make_uint4(w[0], w[1], w[2], w[3]);
-                out[i] = rq;
-                p1_consume_any<true>(a, rq, i, sc, p);
+                q[r][u] = i < nvec ? __ldcg(src[r] + i) : make_uint4(0, 0, 0, 0);
             }
-        }
-        if (blockIdx.x == 0 && threadIdx.x < (p.n & 7u)) {   // ragged tail (n % 8)
-            const uint64_t i = (nvec << 3) + threadIdx.x;
-            float f = 0.0f;
-            for (int r = 0; r < NR; ++r) f = __fadd_rn(f, h2f(p.gsrc[r][p.offset + i]));
-            const uint16_t h = f2h(f);
-            p.g16_out[i] = h;
-            p1_consume1(a, h, i, sc, p);
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const uint64_t i = base + u * stride;
+            if (i >= nvec) continue;
+            float acc[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
+#pragma unroll
+            for (int r = 0; r < NR; ++r) {                 // rank order
+                const uint32_t w[4] = {q[r][u].x, q[r][u].y, q[r][u].z, q[r][u].w};
+#pragma unroll
+                for (int j = 0; j < 8; ++j)
+                    acc[j] = __fadd_rn(acc[j], h2f((j & 1) ? hi16(w[j >> 1]) : lo16(w[j >> 1])));
+            }
+            uint32_t w[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) w[k] = pack16(f2h(acc[2 * k]), f2h(acc[2 * k + 1]));
+            const uint4 rq = make_uint4(w[0], w[1], w[2], w[3]);
+            out[i] = rq;
+            p1_consume<KEEP, POW2>(a, rq, i, sc, p);
         }
     }
+}
+
+template <int NR, int U, int MINB, bool KEEP>
+__global__ void __launch_bounds__(kThreads, MINB) pass1_reduce_nr_kernel(StepParams p) {
+    griddep_launch_dependents();
+    const bool failed = reduce_ready_barrier(p);
+    const P1Scale sc = p1_scale(p);
+    P1Acc a;
+    if (!failed) {
+        if (sc.pow2) reduce_stream_nr<NR, U, KEEP, true>(a, sc, p);
+        else reduce_stream_nr<NR, U, KEEP, false>(a, sc, p);
+        reduce_tail(a, sc, p);
+    }
     p1_finish(a, sc, failed, p);
+}
+
+// ark_cuda_opt_weights_wait: one warp; lane r waits, bounded, for rank r's
+// weights-ready epoch of the last step (published by the last block of its
+// pass 2 after its stores into this rank's weight buffer).  On a timeout
+// the state reports ARK_E_TIMEOUT.
+__global__ void weights_wait_kernel(StepParams p) {
+    const int lane = threadIdx.x;
+    const unsigned long long epoch = p.st->steps_called;   // the step just run
+    bool ok = true;
+    if (lane < p.world && epoch > 0) {
+        const uint64_t* w = slot_of(p.xchg, epoch, p.world, lane) + kSlotWeightsReady;
+        const uint64_t t0 = global_ns();
+        while (ld_acquire_sys(w) != epoch) {
+            if (global_ns() - t0 > p.peer_timeout_ns) {
+                ok = false;
+                break;
+            }
+            __nanosleep(64);
+        }
+    }
+    if (!__all_sync(0xFFFFFFFFu, ok) && lane == 0) p.st->error = ARK_E_TIMEOUT;
+}
+
+// The logits-gradient check and loss scaling (training.rs:228-245): counts
+// the non-finite values of the unscaled logits gradients and multiplies
+// every element by the current loss scale in place (x *= loss_scale, one
+// f32 multiply, :244-245).  The count goes into the state's logits_bad word,
+// which the next step's pass 1 folds into its non-finite partial.  One pass
+// (4 B read + 4 B written per element): on a step the check rejects, the
+// reference returns before scaling and discards the buffer, so its contents
+// are not part of the result.
+constexpr int kLogitsU = 4;
+__device__ __forceinline__ unsigned int f32_nonfinite(float f) {
+    return (__float_as_uint(f) & 0x7F800000u) == 0x7F800000u;
+}
+
+__global__ void __launch_bounds__(kThreads) logits_kernel(float* __restrict__ x, uint64_t n,
+                                                          const ark_opt_status* __restrict__ st,
+                                                          unsigned long long* bad_out) {
+    __shared__ unsigned long long s_bad[kThreads / 32];
+    const float scale = st->loss_scale;
+    const uint64_t stride = (uint64_t)gridDim.x * kThreads;
+    unsigned int bad = 0;
+    if (((uintptr_t)x & 15u) == 0) {
+        const uint64_t nq = n >> 2;
+        float4* x4 = reinterpret_cast<float4*>(x);
+        for (uint64_t base = (uint64_t)blockIdx.x * kThreads + threadIdx.x; base < nq;
+             base += stride * kLogitsU) {
+            float4 q[kLogitsU];
+#pragma unroll
+            for (int u = 0; u < kLogitsU; ++u) {
+                const uint64_t i = base + u * stride;
+                if (i < nq) q[u] = ld_stream(x4 + i);
+            }
+#pragma unroll
+            for (int u = 0; u < kLogitsU; ++u) {
+                const uint64_t i = base + u * stride;
+                if (i >= nq) continue;
+                bad += f32_nonfinite(q[u].x) + f32_nonfinite(q[u].y) + f32_nonfinite(q[u].z) +
+                       f32_nonfinite(q[u].w);
+                q[u].x = __fmul_rn(q[u].x, scale);
+                q[u].y = __fmul_rn(q[u].y, scale);
+                q[u].z = __fmul_rn(q[u].z, scale);
+                q[u].w = __fmul_rn(q[u].w, scale);
+                st_stream(x4 + i, q[u]);
+            }
+        }
+        if (blockIdx.x == 0 && threadIdx.x < (n & 3u)) {
+            const uint64_t i = (nq << 2) + threadIdx.x;
+            bad += f32_nonfinite(x[i]);
+            x[i] = __fmul_rn(x[i], scale);
+        }
+    } else {
+        for (uint64_t i = (uint64_t)blockIdx.x * kThreads + threadIdx.x; i < n; i += stride) {
+            bad += f32_nonfinite(x[i]);
+            x[i] = __fmul_rn(x[i], scale);
+        }
+    }
+    const unsigned long long b = block_sum_u64<kThreads>(bad, s_bad);
+    if (threadIdx.x == 0 && b) atomicAdd(bad_out, b);
 }
 
 // Launch-shape variants, selected at init by shard size (or by index through
@@ -777,13 +957,14 @@ static const Pass1Variant kPass1Variants[] = {
 };
 #undef ARK_P1
 // reduce-scatter pass 1 by rank count (any other count: the generic kernel)
+template <bool KEEP>
 static Pass1Fn pass1_reduce_for(int world) {
     switch (world) {
-        case 1: return pass1_reduce_nr_kernel<1, 8, 4>;
-        case 2: return pass1_reduce_nr_kernel<2, 4, 4>;
-        case 4: return pass1_reduce_nr_kernel<4, 2, 4>;
-        case 8: return pass1_reduce_nr_kernel<8, 1, 4>;
-        default: return pass1_reduce_kernel<2, 4>;
+        case 1: return pass1_reduce_nr_kernel<1, 8, 4, KEEP>;
+        case 2: return pass1_reduce_nr_kernel<2, 4, 4, KEEP>;
+        case 4: return pass1_reduce_nr_kernel<4, 2, 4, KEEP>;
+        case 8: return pass1_reduce_nr_kernel<8, 1, 4, KEEP>;
+        default: return pass1_reduce_kernel<2, 4, KEEP>;
     }
 }
 #define ARK_P2(U, B)                                                                     \
@@ -804,6 +985,13 @@ static const Pass2Variant kPass2Variants[] = {
 };
 #undef ARK_P2X
 #undef ARK_P2
+// Pass 2 with the fused weight all-gather, [shape][kept range non-empty]:
+// shape 0 is 1 group x 3 blocks/SM (shards below 100M params), shape 1 is
+// 2 groups x 2 blocks/SM, as for the plain kernel.
+static const Pass2Fn kPass2Gather[2][2] = {
+    {pass2_kernel<1, 3, false, false, 1, true>, pass2_kernel<1, 3, false, true, 1, true>},
+    {pass2_kernel<2, 2, false, false, 1, true>, pass2_kernel<2, 2, false, true, 1, true>},
+};
 
 }  // namespace ark
 
@@ -826,10 +1014,13 @@ struct ark_opt_state {
     unsigned int* d_tickets = nullptr;
     Partial* d_part_local = nullptr;
     Partial* d_part_all = nullptr;
+    unsigned long long* d_verdict = nullptr;     // pass-2 exchange verdict word
+    unsigned long long* d_logits_bad = nullptr;  // non-finite logits count since the last step
     ark_opt_status* h_status = nullptr;  // pinned
     int blocks1 = 0, blocks2 = 0, blocks1r = 0;
     Pass1Fn pass1 = nullptr, pass1r = nullptr;   // chosen launch-shape variants
-    Pass2Fn pass2 = nullptr, pass2_w32 = nullptr;
+    Pass2Fn pass2 = nullptr, pass2_w32 = nullptr, pass2_gather = nullptr;
+    int blocks2g = 0;
     bool pdl = false;  // pass 2 launched as a programmatic dependent of pass 1
     int blocks2w = 0;
     // P2P exchange slots (world > 1)
@@ -842,6 +1033,11 @@ struct ark_opt_state {
     uint64_t gbuf_n = 0;
     std::vector<void*> gpeer;                 // every rank's buffer, mapped here
     const uint16_t** d_gsrc = nullptr;        // device copy of gpeer
+    // full-weight buffers of the fused weight all-gather (world >= 1)
+    void* wbuf = nullptr;                     // this rank's buffer (cudaMalloc, IPC-exported)
+    uint64_t wbuf_n = 0;
+    std::vector<void*> wpeer;                 // every rank's buffer, mapped here
+    uint16_t** d_wdst = nullptr;              // device copy of wpeer
     uint64_t timeout_ns = 0;
     // graph replay
     // graph replay: slot 0 plain, slot 1 with four event-record nodes that are
@@ -849,7 +1045,7 @@ struct ark_opt_state {
     // (slots 2 and 3: the same for the reduce-scatter step)
     cudaGraph_t gsrc[4] = {nullptr, nullptr, nullptr, nullptr};
     cudaGraphExec_t gexec[4] = {nullptr, nullptr, nullptr, nullptr};
-    const void* gkey[4][5] = {};
+    const void* gkey[4][6] = {};
     cudaGraphNode_t ev_node[2][4] = {};     // per profiled slot (1, 3)
     cudaEvent_t ph_ev[4] = {nullptr, nullptr, nullptr, nullptr};   // capture placeholders
     cudaStream_t capture_stream = nullptr;
@@ -945,7 +1141,7 @@ int share_ipc(ark_opt_state* s, void* local, std::vector<void*>& mapped, bool* a
 int setup_p2p(ark_opt_state* s) {
     const int W = s->cfg.world_size;
     if (W < 2 || W > kMaxP2PRanks || !s->comm) return ARK_OK;
-    const size_t slot_bytes = sizeof(uint64_t) * 4 * 2 * (size_t)W;
+    const size_t slot_bytes = sizeof(uint64_t) * kSlotWords * 2 * (size_t)W;
     if (cudaMalloc(&s->xchg, slot_bytes) != cudaSuccess) s->xchg = nullptr;
     else if (cudaMemset(s->xchg, 0, slot_bytes) != cudaSuccess) return ARK_E_CUDA;
     std::vector<void*> mapped;
@@ -975,15 +1171,63 @@ void teardown_p2p(ark_opt_state* s) {
     s->p2p = false;
 }
 
+// A buffer of every rank mapped into every other rank: close the peers'
+// mappings, free this rank's allocation and the device pointer table.
+template <typename T>
+void release_shared(void*& local, std::vector<void*>& mapped, T**& d_table) {
+    for (size_t r = 0; r < mapped.size(); ++r)
+        if (mapped[r] && mapped[r] != local) cudaIpcCloseMemHandle(mapped[r]);
+    mapped.clear();
+    if (d_table) cudaFree(d_table);
+    if (local) cudaFree(local);
+    d_table = nullptr;
+    local = nullptr;
+}
+
+// Collective over the rank's communicator (every rank calls it): allocate
+// `bytes` here (zeroed), map every rank's allocation into this process
+// (world > 1: CUDA IPC, needs the mapped exchange slots) and copy the
+// rank-ordered pointer table to the device.  On failure nothing is kept.
+template <typename T>
+int make_shared(ark_opt_state* s, size_t bytes, void*& local, std::vector<void*>& mapped,
+                T**& d_table) {
+    const int W = s->cfg.world_size;
+    if (W > 1 && !s->p2p) return ARK_E_UNSUPPORTED;
+    release_shared(local, mapped, d_table);
+    bytes = (bytes + 255) & ~size_t(255);
+    if (cudaMalloc(&local, bytes) != cudaSuccess) {
+        local = nullptr;
+        if (W == 1) return ARK_E_CUDA;   // else share_ipc reports it to every rank
+    } else if (cudaMemset(local, 0, bytes) != cudaSuccess) {
+        return ARK_E_CUDA;
+    }
+    if (W == 1) {
+        mapped.assign(1, local);
+    } else {
+        bool all_ok = false;
+        const int rc = share_ipc(s, local, mapped, &all_ok);
+        if (rc || !all_ok) {
+            release_shared(local, mapped, d_table);
+            return rc ? rc : ARK_E_UNSUPPORTED;
+        }
+    }
+    if (cudaMalloc(&d_table, sizeof(T*) * W) != cudaSuccess ||
+        cudaMemcpy(d_table, mapped.data(), sizeof(T*) * W, cudaMemcpyHostToDevice) !=
+            cudaSuccess) {
+        release_shared(local, mapped, d_table);
+        return ARK_E_CUDA;
+    }
+    return ARK_OK;
+}
+
 void teardown_grads(ark_opt_state* s) {
-    for (size_t r = 0; r < s->gpeer.size(); ++r)
-        if (s->gpeer[r] && s->gpeer[r] != s->gbuf) cudaIpcCloseMemHandle(s->gpeer[r]);
-    s->gpeer.clear();
-    if (s->d_gsrc) cudaFree(s->d_gsrc);
-    if (s->gbuf) cudaFree(s->gbuf);
-    s->d_gsrc = nullptr;
-    s->gbuf = nullptr;
+    release_shared(s->gbuf, s->gpeer, s->d_gsrc);
     s->gbuf_n = 0;
+}
+
+void teardown_weights(ark_opt_state* s) {
+    release_shared(s->wbuf, s->wpeer, s->d_wdst);
+    s->wbuf_n = 0;
 }
 
 StepParams make_params(const ark_opt_state* s, const uint16_t* g16) {
@@ -1025,6 +1269,10 @@ StepParams make_params(const ark_opt_state* s, const uint16_t* g16) {
     p.ticket2 = s->d_tickets + 1;
     p.part_local = s->d_part_local;
     p.part_all = s->d_part_all;
+    p.verdict = s->d_verdict;
+    p.logits_bad = s->d_logits_bad;
+    p.wdst = s->d_wdst;
+    p.wself = 1;
     return p;
 }
 
@@ -1054,10 +1302,12 @@ cudaError_t launch_pass2(Pass2Fn fn, int blocks, cudaStream_t stream, bool pdl,
 
 int enqueue_step(ark_opt_state* s, cudaStream_t stream, uint16_t* w16, const uint16_t* g16,
                  float* m, float* v, float* w32, cudaEvent_t* ev, bool capturing = false,
-                 bool reduce = false) {
+                 bool reduce = false, bool gather = false) {
     StepParams p = make_params(s, g16);
     if (reduce) p.g16_out = const_cast<uint16_t*>(g16);
     p.w32_out = w32;
+    // the caller's shard may live inside this rank's full weight buffer
+    p.wself = !(gather && w16 == static_cast<uint16_t*>(s->wbuf) + s->cfg.shard_offset);
     if (ev) ARK_RECORD(ev[0], stream);
     if (reduce) s->pass1r<<<s->blocks1r, kThreads, 0, stream>>>(p);
     else s->pass1<<<s->blocks1, kThreads, 0, stream>>>(p);
@@ -1074,6 +1324,8 @@ int enqueue_step(ark_opt_state* s, cudaStream_t stream, uint16_t* w16, const uin
     if (ev) ARK_RECORD(ev[2], stream);
     const bool pdl = s->pdl && !ev && (s->cfg.world_size == 1 || s->p2p);
     if (w32) ARK_CUDA_TRY(launch_pass2(s->pass2_w32, s->blocks2w, stream, pdl, p, w16, m, v));
+    else if (gather)
+        ARK_CUDA_TRY(launch_pass2(s->pass2_gather, s->blocks2g, stream, pdl, p, w16, m, v));
     else ARK_CUDA_TRY(launch_pass2(s->pass2, s->blocks2, stream, pdl, p, w16, m, v));
     if (ev) ARK_RECORD(ev[3], stream);
     return ARK_OK;
@@ -1089,7 +1341,7 @@ void drop_graph(ark_opt_state* s, int slot) {
 // Capture one step into graph slot 0 (plain) or 1 (with event-record nodes
 // on placeholder events, whose nodes are then located for retargeting).
 int capture_graph(ark_opt_state* s, int slot, uint16_t* w16, const uint16_t* g16, float* m,
-                  float* v, float* w32) {
+                  float* v, float* w32, bool gather) {
     const bool profiled = slot & 1, reduce = slot >= 2;
     drop_graph(s, slot);
     // capture on a private stream (the legacy default stream cannot be
@@ -1101,7 +1353,7 @@ int capture_graph(ark_opt_state* s, int slot, uint16_t* w16, const uint16_t* g16
     cudaGraph_t g = nullptr;
     ARK_CUDA_TRY(cudaStreamBeginCapture(s->capture_stream, cudaStreamCaptureModeThreadLocal));
     const int rc = enqueue_step(s, s->capture_stream, w16, g16, m, v, w32,
-                                profiled ? s->ph_ev : nullptr, true, reduce);
+                                profiled ? s->ph_ev : nullptr, true, reduce, gather);
     const cudaError_t e = cudaStreamEndCapture(s->capture_stream, &g);
     if (rc != ARK_OK) {
         if (g) cudaGraphDestroy(g);
@@ -1128,7 +1380,7 @@ int capture_graph(ark_opt_state* s, int slot, uint16_t* w16, const uint16_t* g16
             if (!evn[j]) return ARK_E_CUDA;
     }
     ARK_CUDA_TRY(cudaGraphInstantiate(&s->gexec[slot], g, 0));
-    const void* key[5] = {w16, g16, m, v, w32};
+    const void* key[6] = {w16, g16, m, v, w32, gather ? s->wbuf : nullptr};
     memcpy(s->gkey[slot], key, sizeof(key));
     return ARK_OK;
 }
@@ -1201,7 +1453,12 @@ int ark_cuda_opt_init(const ark_opt_cfg* cfg, ark_opt_state** out) {
     s->pass2_w32 = kPass2Variants[varw].fn_w32[keep];
     s->blocks2w = streaming_grid(reinterpret_cast<const void*>(s->pass2_w32), kThreads, 0,
                                  (cfg->n >> 3) / kPass2Variants[varw].unroll + 1);
-    s->pass1r = pass1_reduce_for(cfg->world_size);
+    s->pass1r = keep ? pass1_reduce_for<true>(cfg->world_size)
+                     : pass1_reduce_for<false>(cfg->world_size);
+    const int shape_g = cfg->n < 100000000ull ? 0 : 1;
+    s->pass2_gather = kPass2Gather[shape_g][keep];
+    s->blocks2g = streaming_grid(reinterpret_cast<const void*>(s->pass2_gather), kThreads, 0,
+                                 (cfg->n >> 3) / (shape_g ? 2 : 1) + 1);
     s->blocks1r = streaming_grid(reinterpret_cast<const void*>(s->pass1r), kThreads, 0,
                                  (cfg->n >> 3) + 1);
     s->blocks2 = streaming_grid(reinterpret_cast<const void*>(s->pass2), kThreads, 0,
@@ -1223,6 +1480,8 @@ int ark_cuda_opt_init(const ark_opt_cfg* cfg, ark_opt_state** out) {
     const size_t o_tk = take(sizeof(unsigned int) * 2);
     const size_t o_pl = take(sizeof(Partial));
     const size_t o_pa = take(sizeof(Partial) * W);
+    const size_t o_vd = take(sizeof(unsigned long long));
+    const size_t o_lb = take(sizeof(unsigned long long));
     if (cudaMalloc(&s->dmem, off) != cudaSuccess) {
         ark_cuda_opt_destroy(s);
         return ARK_E_CUDA;
@@ -1235,6 +1494,8 @@ int ark_cuda_opt_init(const ark_opt_cfg* cfg, ark_opt_state** out) {
     s->d_tickets = reinterpret_cast<unsigned int*>(base + o_tk);
     s->d_part_local = reinterpret_cast<Partial*>(base + o_pl);
     s->d_part_all = reinterpret_cast<Partial*>(base + o_pa);
+    s->d_verdict = reinterpret_cast<unsigned long long*>(base + o_vd);
+    s->d_logits_bad = reinterpret_cast<unsigned long long*>(base + o_lb);
     // single-GPU: pass 1 writes the rank partial straight into the gathered slot
     if (W == 1) s->d_part_local = s->d_part_all;
     if (cudaMallocHost(&s->h_status, sizeof(ark_opt_status)) != cudaSuccess) {
@@ -1270,7 +1531,7 @@ int ark_cuda_opt_init(const ark_opt_cfg* cfg, ark_opt_state** out) {
 }
 
 static int run_step(ark_opt_state* s, uint16_t* w16, const uint16_t* g16, float* m, float* v,
-                    float* w32, bool reduce) {
+                    float* w32, bool reduce, bool gather = false) {
     if (!s) return ARK_E_INVALID_ARG;
     if (s->cfg.n && (!w16 || !g16 || !m || !v)) return ARK_E_INVALID_ARG;
     if (!aligned16(w16) || !aligned16(g16) || !aligned16(m) || !aligned16(v) || !aligned16(w32))
@@ -1280,18 +1541,24 @@ static int run_step(ark_opt_state* s, uint16_t* w16, const uint16_t* g16, float*
         if (s->cfg.shard_offset + s->cfg.n > s->gbuf_n) return ARK_E_INVALID_ARG;
         if ((s->cfg.shard_offset & 7u) != 0) return ARK_E_MISALIGNED;
     }
+    if (gather) {
+        if (!s->wbuf) return ARK_E_INVALID_ARG;          // no ark_cuda_opt_weight_buffer yet
+        if (s->cfg.shard_offset + s->cfg.n > s->wbuf_n) return ARK_E_INVALID_ARG;
+        if ((s->cfg.shard_offset & 7u) != 0) return ARK_E_MISALIGNED;
+        if (w32) return ARK_E_UNSUPPORTED;               // one option or the other
+    }
     DeviceGuard dg(s->device);
     const bool profile = s->prof_used < s->prof_cap;
     cudaEvent_t* ev = profile ? &s->prof_events[4 * s->prof_used] : nullptr;
     if (!(s->cfg.flags & ARK_OPT_USE_GRAPH)) {
-        const int rc = enqueue_step(s, s->stream, w16, g16, m, v, w32, ev, false, reduce);
+        const int rc = enqueue_step(s, s->stream, w16, g16, m, v, w32, ev, false, reduce, gather);
         if (rc == ARK_OK && profile) s->prof_used++;
         return rc;
     }
     const int slot = (reduce ? 2 : 0) + (profile ? 1 : 0);
-    const void* key[5] = {w16, g16, m, v, w32};
+    const void* key[6] = {w16, g16, m, v, w32, gather ? s->wbuf : nullptr};
     if (!s->gexec[slot] || memcmp(key, s->gkey[slot], sizeof(key)) != 0) {
-        const int rc = capture_graph(s, slot, w16, g16, m, v, w32);
+        const int rc = capture_graph(s, slot, w16, g16, m, v, w32, gather);
         if (rc != ARK_OK) {
             drop_graph(s, slot);
             return rc;
@@ -1317,43 +1584,65 @@ int ark_cuda_opt_step_reduce(ark_opt_state* s, uint16_t* w16, uint16_t* g16_shar
 
 int ark_cuda_opt_step_ex(ark_opt_state* s, uint16_t* w16, uint16_t* g16, float* m, float* v,
                          float* w32_out, uint32_t options) {
-    if (options & ~ARK_STEP_REDUCE) return ARK_E_INVALID_ARG;
-    return run_step(s, w16, g16, m, v, w32_out, (options & ARK_STEP_REDUCE) != 0);
+    if (options & ~(ARK_STEP_REDUCE | ARK_STEP_GATHER_WEIGHTS)) return ARK_E_INVALID_ARG;
+    return run_step(s, w16, g16, m, v, w32_out, (options & ARK_STEP_REDUCE) != 0,
+                    (options & ARK_STEP_GATHER_WEIGHTS) != 0);
 }
 
 int ark_cuda_opt_grad_buffer(ark_opt_state* s, uint64_t n_full, uint16_t** out) {
     if (!s || !out || n_full == 0) return ARK_E_INVALID_ARG;
     *out = nullptr;
     if (s->cfg.shard_offset + s->cfg.n > n_full) return ARK_E_INVALID_ARG;
-    const int W = s->cfg.world_size;
-    if (W > 1 && !s->p2p) return ARK_E_UNSUPPORTED;      // needs the mapped exchange slots
     DeviceGuard dg(s->device);
     teardown_grads(s);
-    const size_t bytes = ((n_full * sizeof(uint16_t)) + 255) & ~size_t(255);
-    if (cudaMalloc(&s->gbuf, bytes) != cudaSuccess) {
-        s->gbuf = nullptr;
-        if (W == 1) return ARK_E_CUDA;
-    } else if (cudaMemset(s->gbuf, 0, bytes) != cudaSuccess) {
-        return ARK_E_CUDA;
-    }
-    if (W == 1) {
-        s->gpeer.assign(1, s->gbuf);
-    } else {
-        bool all_ok = false;
-        const int rc = share_ipc(s, s->gbuf, s->gpeer, &all_ok);
-        if (rc || !all_ok) {
-            teardown_grads(s);
-            return rc ? rc : ARK_E_UNSUPPORTED;
-        }
-    }
-    if (cudaMalloc(&s->d_gsrc, sizeof(uint16_t*) * W) != cudaSuccess ||
-        cudaMemcpy(s->d_gsrc, s->gpeer.data(), sizeof(uint16_t*) * W, cudaMemcpyHostToDevice) !=
-            cudaSuccess) {
-        teardown_grads(s);
-        return ARK_E_CUDA;
-    }
+    const int rc = make_shared(s, n_full * sizeof(uint16_t), s->gbuf, s->gpeer, s->d_gsrc);
+    if (rc) return rc;
     s->gbuf_n = n_full;
     *out = static_cast<uint16_t*>(s->gbuf);
+    return ARK_OK;
+}
+
+int ark_cuda_opt_weight_buffer(ark_opt_state* s, uint64_t n_full, uint16_t** out) {
+    if (!s || !out || n_full == 0) return ARK_E_INVALID_ARG;
+    *out = nullptr;
+    if (s->cfg.shard_offset + s->cfg.n > n_full) return ARK_E_INVALID_ARG;
+    DeviceGuard dg(s->device);
+    teardown_weights(s);
+    const int rc = make_shared(s, n_full * sizeof(uint16_t), s->wbuf, s->wpeer, s->d_wdst);
+    if (rc) return rc;
+    s->wbuf_n = n_full;
+    *out = static_cast<uint16_t*>(s->wbuf);
+    return ARK_OK;
+}
+
+int ark_cuda_opt_zero_grads(ark_opt_state* s) {
+    if (!s) return ARK_E_INVALID_ARG;
+    if (!s->gbuf) return ARK_E_INVALID_ARG;   // no ark_cuda_opt_grad_buffer yet
+    DeviceGuard dg(s->device);
+    ARK_CUDA_TRY(cudaMemsetAsync(s->gbuf, 0, s->gbuf_n * sizeof(uint16_t), s->stream));
+    return ARK_OK;
+}
+
+int ark_cuda_opt_weights_wait(ark_opt_state* s) {
+    if (!s) return ARK_E_INVALID_ARG;
+    if (!s->wbuf) return ARK_E_INVALID_ARG;   // no ark_cuda_opt_weight_buffer yet
+    if (s->cfg.world_size == 1) return ARK_OK;   // stream order suffices
+    DeviceGuard dg(s->device);
+    const StepParams p = make_params(s, nullptr);
+    weights_wait_kernel<<<1, 32, 0, s->stream>>>(p);
+    ARK_CUDA_TRY(cudaGetLastError());
+    return ARK_OK;
+}
+
+int ark_cuda_opt_logits_check(ark_opt_state* s, float* logits_grad, uint64_t n) {
+    if (!s || (n && !logits_grad)) return ARK_E_INVALID_ARG;
+    if (n == 0) return ARK_OK;
+    DeviceGuard dg(s->device);
+    const int blocks = streaming_grid(reinterpret_cast<const void*>(logits_kernel), kThreads, 0,
+                                      (n >> 2) / kLogitsU + 1);
+    logits_kernel<<<blocks, kThreads, 0, s->stream>>>(logits_grad, n, s->d_state,
+                                                      s->d_logits_bad);
+    ARK_CUDA_TRY(cudaGetLastError());
     return ARK_OK;
 }
 
@@ -1466,6 +1755,7 @@ int ark_cuda_opt_destroy(ark_opt_state* s) {
     cudaStreamSynchronize(s->stream);
     for (int slot = 0; slot < 4; ++slot) drop_graph(s, slot);
     teardown_grads(s);
+    teardown_weights(s);
     for (cudaEvent_t e : s->ph_ev)
         if (e) cudaEventDestroy(e);
     if (s->capture_stream) cudaStreamDestroy(s->capture_stream);

@@ -176,19 +176,61 @@ class Optimizer:
         """This rank's full gradient buffer for step_reduce (FP16, all
         n_full global elements, zeroed), as a CUDA tensor over library
         memory.  Collective: every rank calls it."""
-        import torch
         n_full = self.layout.n if n_full is None else int(n_full)
         p = ctypes.c_void_p()
         _lib.check("ark_cuda_opt_grad_buffer",
                    _lib.lib().ark_cuda_opt_grad_buffer(self._h, n_full, ctypes.byref(p)))
+        self._gbuf = self._device_view(p.value, n_full, "<f2")
+        return self._gbuf
+
+    def _device_view(self, ptr, n, typestr):
+        import torch
 
         class _View:
-            __cuda_array_interface__ = {"shape": (n_full,), "typestr": "<f2",
-                                        "data": (p.value, False), "version": 3,
-                                        "strides": None}
+            __cuda_array_interface__ = {"shape": (n,), "typestr": typestr, "data": (ptr, False),
+                                        "version": 3, "strides": None}
 
-        self._gbuf = torch.as_tensor(_View(), device=torch.device("cuda", self._cfg.device))
-        return self._gbuf
+        return torch.as_tensor(_View(), device=torch.device("cuda", self._cfg.device))
+
+    def weight_buffer(self, n_full: int | None = None):
+        """This rank's full FP16 weight buffer for step_gather (all n_full
+        global elements, zeroed), as a CUDA tensor over library memory,
+        mapped into every rank.  Collective: every rank calls it."""
+        n_full = self.layout.n if n_full is None else int(n_full)
+        p = ctypes.c_void_p()
+        _lib.check("ark_cuda_opt_weight_buffer",
+                   _lib.lib().ark_cuda_opt_weight_buffer(self._h, n_full, ctypes.byref(p)))
+        self._wbuf = self._device_view(p.value, n_full, "<f2")
+        return self._wbuf
+
+    def step_gather(self, w16, g16, m, v, reduce: bool = False):
+        """step_all (or step_reduce) fused with the ZeRO-1 weight all-gather:
+        the update kernel also stores the updated shard into every rank's
+        weight_buffer().  w16 may be this rank's slice of that buffer."""
+        opts = _lib.ARK_STEP_GATHER_WEIGHTS | (_lib.ARK_STEP_REDUCE if reduce else 0)
+        rc = _lib.lib().ark_cuda_opt_step_ex(
+            self._h, _ptr(w16, "f16", self.n), _ptr(g16, "f16", self.n), _ptr(m, "f32", self.n),
+            _ptr(v, "f32", self.n), None, opts)
+        _lib.check("ark_cuda_opt_step_ex", rc)
+
+    def weights_wait(self):
+        """Order this stream's next work after every rank's stores of the
+        last step_gather into this rank's weight_buffer() (bounded wait)."""
+        _lib.check("ark_cuda_opt_weights_wait", _lib.lib().ark_cuda_opt_weights_wait(self._h))
+
+    def logits_check(self, logits_grad):
+        """training.rs:228-245 on the device: count non-finite logits
+        gradients (FP32 CUDA tensor) and multiply them in place by the
+        current loss scale; a non-finite value makes the next step a skipped
+        overflow step.  Asynchronous."""
+        n = logits_grad.numel()
+        _lib.check("ark_cuda_opt_logits_check", _lib.lib().ark_cuda_opt_logits_check(
+            self._h, _ptr(logits_grad, "f32", n), n))
+
+    def zero_grads(self):
+        """Zero this rank's grad_buffer() on the step's stream
+        (memory.rs:338-342), for a backward that accumulates with +=."""
+        _lib.check("ark_cuda_opt_zero_grads", _lib.lib().ark_cuda_opt_zero_grads(self._h))
 
     def step_reduce(self, w16, g16_shard, m, v):
         """One step on the sum over ranks of every rank's grad_buffer():

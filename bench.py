@@ -57,17 +57,15 @@ def measured_peak():
         return 6650.0, "fallback 6.65 TB/s (MEASURED_PEAKS.json absent)"
 
 
-def kernel_traffic_per_param(summary):
-    """DRAM bytes per parameter of a kernel from its committed ncu summary
-    (profiles/<summary>, line 'dram_bytes_per_param: X')."""
-    p = os.path.join(ROOT, "profiles", summary)
-    try:
-        for line in open(p):
-            if line.strip().startswith("dram_bytes_per_param:"):
-                return float(line.split(":")[1].split()[0])
-    except OSError:
-        pass
-    return None
+# DRAM bytes (read + write) per parameter of one pass-2 launch, from one ncu
+# capture of the default pass-2 kernel on a 128 Mi-param flat case (state
+# above the L2), scaled by the shard's parameters for roofline.traffic:
+#   ncu --metrics dram__bytes_read.sum,dram__bytes_write.sum,gpu__time_duration.sum \
+#       --clock-control none -k regex:pass2_kernel -s 6 -c 1 \
+#       python bench.py --params 134217728 --steps 3 --warmup 3 --no-graph (+ no extra legs)
+# Refresh it whenever pass 2 changes.
+PASS2_DRAM_BYTES_PER_PARAM = 21.58
+NVLINK_PEER_COPY_GBS = 770.0  # measured peer copy per direction per GPU on this pool
 
 
 class ClockSampler:
@@ -339,6 +337,331 @@ def measure_aux(opt, L, w16, g16, m, v, stream, args, max_over_ranks, barrier):
     return out
 
 
+def numa_local_cpus(device):
+    """Host CPUs on the GPU's NUMA node (from its PCI address), or None."""
+    import torch
+    try:
+        pr = torch.cuda.get_device_properties(device)
+        bus = "%04x:%02x:%02x.0" % (pr.pci_domain_id, pr.pci_bus_id, pr.pci_device_id)
+        txt = open(f"/sys/bus/pci/devices/{bus}/local_cpulist").read().strip()
+    except (OSError, AttributeError, RuntimeError):
+        return None
+    cpus = set()
+    for part in txt.split(","):
+        a, _, b = part.partition("-")
+        cpus.update(range(int(a), int(b or a) + 1))
+    return cpus or None
+
+
+def timed_loop(fn, k, stream, barrier, max_over_ranks):
+    """k calls of fn between CUDA events on the step's stream; ms per call,
+    max over ranks."""
+    import torch
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(k):
+        fn()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    return max_over_ranks(e0.elapsed_time(e1) / k)
+
+
+def measure_allgather(opt, L, w16, g16, m, v, stream, args, max_over_ranks, barrier):
+    """The optional ZeRO-1 FP16 weight all-gather, timed separately: the
+    NCCL all-gather alone and after the step, and the library's all-gather
+    fused with the update (pass 2 stores the updated shard into every rank's
+    full weight buffer over NVLink, ARK_STEP_GATHER_WEIGHTS)."""
+    import torch
+    world, n, dev = opt.world, opt.n, w16.device
+    k = max(5, min(args.steps, 100))
+    stride = -(-L.n // world) + 128
+    w_pad = torch.zeros(stride, dtype=torch.float16, device=dev)
+    w_pad[:n].copy_(w16)
+    full_nccl = torch.empty(stride * world, dtype=torch.float16, device=dev)
+    t_nccl = timed_loop(lambda: opt.allgather_weights(w_pad, full_nccl, stride), k, stream,
+                        barrier, max_over_ranks)
+
+    def step_then_nccl():
+        opt.step_all(w_pad[:n], g16, m, v)
+        opt.allgather_weights(w_pad, full_nccl, stride)
+
+    t_seq = timed_loop(step_then_nccl, k, stream, barrier, max_over_ranks)
+    del full_nccl
+    full = opt.weight_buffer()                    # collective
+    wf = full[opt.lo:opt.hi]
+    wf.copy_(w_pad[:n])
+
+    def fused():
+        opt.step_gather(wf, g16, m, v)
+        opt.weights_wait()
+
+    for _ in range(3):
+        fused()
+    t_fused = timed_loop(fused, k, stream, barrier, max_over_ranks)
+    t_step = timed_loop(lambda: opt.step_all(w_pad[:n], g16, m, v), k, stream, barrier,
+                        max_over_ranks)
+    bytes_in = 2 * (L.n - n)                      # every other rank's shard, into this GPU
+    out = {"bytes_in_per_gpu": int(bytes_in), "steps": k,
+           "nccl_allgather_ms": round(t_nccl, 4),
+           "nccl_gbs_in_per_gpu": round(bytes_in / (t_nccl * 1e-3) / 1e9, 1),
+           "step_ms": round(t_step, 4),
+           "step_then_nccl_ms": round(t_seq, 4),
+           "fused_step_gather_ms": round(t_fused, 4),
+           "fused_gbs_in_per_gpu": round(bytes_in / (t_fused * 1e-3) / 1e9, 1),
+           "peer_copy_gbs_measured": NVLINK_PEER_COPY_GBS,
+           "fused_nvlink_frac": round(bytes_in / (t_fused * 1e-3) / 1e9 / NVLINK_PEER_COPY_GBS, 4),
+           "nccl_nvlink_frac": round(bytes_in / (t_nccl * 1e-3) / 1e9 / NVLINK_PEER_COPY_GBS, 4),
+           "fused_saving_vs_step_then_nccl_ms": round(t_seq - t_fused, 4),
+           "how": "CUDA events over k iterations on the step's stream, max over ranks; fused = "
+                  "step with ARK_STEP_GATHER_WEIGHTS + ark_cuda_opt_weights_wait"}
+    full_ok = bool(torch.equal(full[opt.lo:opt.hi].view(torch.int16), wf.view(torch.int16)))
+    out["own_slice_consistent"] = full_ok
+    return out
+
+
+LEGACY_KERNEL_N = 1 << 27     # elements per legacy-kernel measurement (state >> L2)
+
+
+def measure_legacy(L, stream, args):
+    """The drop-in path: the reference's per-tensor optimizer calls through
+    the unchanged legacy symbols (272 x ark_asm_adam_step_f16 per EKO step,
+    optimizer.rs:185-227, in the library's async mode with one wait per
+    step), and each legacy kernel alone at 2^27 elements, as GB/s of its
+    algorithmic bytes."""
+    import torch
+
+    import ark_b200 as ab
+    from ark_b200 import synth
+    dev = torch.device("cuda", torch.cuda.current_device())
+    n = L.n
+    w16 = torch.empty(n, dtype=torch.float16, device=dev)
+    g32 = torch.empty(n, dtype=torch.float32, device=dev)
+    m = torch.empty(n, dtype=torch.float32, device=dev)
+    v = torch.empty(n, dtype=torch.float32, device=dev)
+    synth.fill_f16(w16, 0, SEED, synth.STREAM_W, 0.02)
+    synth.fill_f32(g32, 0, SEED, 9, 1e-3)
+    synth.fill_f32(m, 0, SEED, synth.STREAM_M, 1e-4)
+    synth.fill_f32(v, 0, SEED, synth.STREAM_V, 1e-3, square=True)
+    lib = ab.lib()
+    hp = EKO_HPARAMS
+    calls = []
+    o = 0
+    for t in L.tensors:                          # reference order, per-tensor wd
+        wd = hp["weight_decay"] if t.decay else 0.0
+        calls.append((w16.data_ptr() + 2 * o, g32.data_ptr() + 4 * o, m.data_ptr() + 4 * o,
+                      v.data_ptr() + 4 * o, t.numel, wd))
+        o += t.numel
+    step_no = [START_STEP]
+
+    def legacy_step():
+        t = step_no[0]
+        for wp, gp, mp, vp, cnt, wd in calls:
+            lib.ark_asm_adam_step_f16(wp, gp, mp, vp, cnt, hp["lr"], hp["beta1"], hp["beta2"],
+                                      hp["eps"], wd, t)
+        step_no[0] += 1
+
+    nothing = lambda: None  # noqa: E731
+    ab.legacy_set_async(True)
+    try:
+        for _ in range(3):
+            legacy_step()
+        ab.legacy_sync()
+        k = max(3, min(args.steps, 50))
+        t_leg = timed_loop(legacy_step, k, stream, nothing, lambda x: x)
+        assert lib.ark_cuda_last_error() == 0
+        # the same 272 calls captured once into a CUDA graph (the legacy
+        # stream pointed at a capturing stream) and replayed: t is fixed in
+        # the captured launches, which changes nothing in the time
+        t_graph = None
+        cap = torch.cuda.Stream(device=dev)
+        graph = torch.cuda.CUDAGraph()
+        lib.ark_cuda_legacy_set_stream(cap.cuda_stream)
+        try:
+            with torch.cuda.graph(graph, stream=cap):
+                legacy_step()
+        finally:
+            lib.ark_cuda_legacy_set_stream(None)
+        if lib.ark_cuda_last_error() == 0:
+            for _ in range(3):
+                graph.replay()
+            t_graph = timed_loop(graph.replay, k, torch.cuda.current_stream(dev), nothing,
+                                 lambda x: x)
+        del graph
+        del w16, g32, m, v
+        torch.cuda.empty_cache()
+        # each kernel alone
+        N = LEGACY_KERNEL_N
+        a32 = torch.empty(N, dtype=torch.float32, device=dev)
+        b32 = torch.empty(N, dtype=torch.float32, device=dev)
+        c32 = torch.empty(N, dtype=torch.float32, device=dev)
+        d32 = torch.empty(N, dtype=torch.float32, device=dev)
+        h16 = torch.empty(N, dtype=torch.float16, device=dev)
+        synth.fill_f32(a32, 0, 1, 5, 0.02)
+        synth.fill_f32(b32, 0, 1, 9, 1e-3)
+        synth.fill_f32(c32, 0, 1, 3, 1e-4)
+        synth.fill_f32(d32, 0, 1, 4, 1e-3, square=True)
+        synth.fill_f16(h16, 0, 1, 1, 0.02)
+        norm = torch.zeros(1, dtype=torch.float32, device=dev)
+        sh = stream.cuda_stream
+        kk = 20
+        clip_no = [0]
+
+        def clip_call():
+            # the norm starts near 11.6 and each call clips it to a threshold
+            # half the previous one, so every call applies the scale
+            thr = 8.0 * 0.5 ** clip_no[0]
+            clip_no[0] += 1
+            lib.ark_cuda_grad_clip_noalloc(b32.data_ptr(), N, thr, norm.data_ptr(), sh)
+
+        kern = {
+            "adam_vec8_kernel<f16> (ark_asm_adam_step_f16)": (24, lambda: lib.ark_asm_adam_step_f16(
+                h16.data_ptr(), b32.data_ptr(), c32.data_ptr(), d32.data_ptr(), N, 3e-4, 0.9,
+                0.95, 1e-8, 0.1, 1000)),
+            "adam_vec8_kernel<f32> (ark_asm_adam_step)": (32, lambda: lib.ark_asm_adam_step(
+                a32.data_ptr(), b32.data_ptr(), c32.data_ptr(), d32.data_ptr(), N, 3e-4, 0.9,
+                0.95, 1e-8, 0.1, 1000)),
+            "clip_norm_kernel + clip_scale_kernel (grad clip, scale applied)": (
+                12, clip_call),
+            "quant_kernel (ark_quant_f32_to_f16)": (6, lambda: lib.ark_quant_f32_to_f16(
+                a32.data_ptr(), h16.data_ptr(), N)),
+            "dequant_kernel (ark_dequant_f16_to_f32)": (6, lambda: lib.ark_dequant_f16_to_f32(
+                h16.data_ptr(), a32.data_ptr(), N)),
+        }
+        per = {}
+        for name, (bpe, fn) in kern.items():
+            for _ in range(3):
+                fn()
+            ms = timed_loop(fn, kk, stream, nothing, lambda x: x)
+            per[name] = {"ms": round(ms, 4), "bytes_per_elem": bpe,
+                         "gbs": round(bpe * N / (ms * 1e-3) / 1e9, 1)}
+        assert lib.ark_cuda_last_error() == 0
+    finally:
+        ab.legacy_set_async(False)
+    peak, _ = measured_peak()
+    for d in per.values():
+        d["frac"] = round(d["gbs"] / peak, 4)
+    return {"legacy_step_ms": round(t_leg, 4), "legacy_step_calls": len(calls),
+            "legacy_step_gbs": round(BYTES_PER_PARAM * n / (t_leg * 1e-3) / 1e9, 1),
+            "legacy_step_graph_ms": round(t_graph, 4) if t_graph else None,
+            "legacy_step_note": "272 x ark_asm_adam_step_f16 per step (FP32 grads, already "
+                                "unscaled and clipped: the reference's unscale and clip are "
+                                "host loops with no legacy symbol), async mode, events around "
+                                "the calls",
+            "kernels_elements": N, "kernels": per}
+
+
+def _windows_of_shard(L, lo, hi, span=2048):
+    """Windows of [lo, hi): the shard ends, its middle, the weight-decay
+    boundary and the tensor boundaries that fall inside it."""
+    cand = [lo, hi - span, (lo + hi) // 2, L.n_decay - span // 2]
+    cand += [L.offsets[t.name] - span // 2 for t in L.flat]
+    out = set()
+    for a in cand:
+        a = max(lo, min(a, hi - span))
+        if lo <= a < hi:
+            out.add((a, min(a + span, hi)))
+    return sorted(out)
+
+
+def parity_leg(opt, L, w16, g16, m, v, heavy, world, rank, dev, barrier):
+    """Checker leg, after every timed region: the CPU oracle (test
+    infrastructure, never the measured path) against one fresh device step.
+    Every rank regenerates its shard's inputs, computes its oracle partial
+    sum of squares, and the partials are all-gathered in rank order; each
+    rank then compares windows of its shard (ends, middle, weight-decay and
+    tensor boundaries) bit for bit with the oracle driven by the oracle's
+    own global sum, and the replicated state across ranks."""
+    import torch
+    import torch.distributed as dist
+
+    from ark_b200 import synth
+    from oracle import oracle
+    t0 = time.perf_counter()
+    oracle.build()
+    cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    local_world = int(os.environ.get("LOCAL_WORLD_SIZE", world))
+    oracle.lib().ork_set_threads(max(1, cores // max(local_world, 1)))
+    lo, hi, n = opt.lo, opt.hi, opt.n
+    # fresh inputs in the same buffers (the timed steps have moved w, m, v)
+    synth.fill_f16(w16, lo, SEED, synth.STREAM_W, 0.02)
+    synth.fill_grads(g16, lo, SEED, LOSS_SCALE, heavy=heavy)
+    synth.fill_f32(m, lo, SEED, synth.STREAM_M, 1e-4)
+    synth.fill_f32(v, lo, SEED, synth.STREAM_V, 1e-3, square=True)
+    opt.set_status(opt_step=START_STEP - 1, loss_scale=LOSS_SCALE, clean_steps=0,
+                   consecutive_nans=0, last_overflow=0, early_stop=0, error=0,
+                   skipped_steps=0)
+    g_host = oracle.synth_f16(n, lo, SEED, synth.STREAM_G, 1e-3, LOSS_SCALE,
+                              synth.HEAVY_EVERY if heavy else 0,
+                              synth.HEAVY_MULT if heavy else 1.0)
+    cfg = oracle.make_cfg(n_decay=L.n_decay, scale_every=2000, scale_max=2.0 ** 24,
+                          **{k: EKO_HPARAMS[k] for k in ("beta1", "beta2", "eps",
+                                                         "weight_decay", "grad_clip")})
+    sumsq, bad = oracle.partial_f16(cfg, oracle.make_state(LOSS_SCALE, START_STEP - 1), g_host,
+                                    lo)
+    if world > 1:
+        parts = [torch.zeros(2, dtype=torch.float64, device=dev) for _ in range(world)]
+        dist.all_gather(parts, torch.tensor([sumsq, float(bad)], dtype=torch.float64,
+                                            device=dev))
+        parts = [p.tolist() for p in parts]
+    else:
+        parts = [[sumsq, float(bad)]]
+    g_sum = 0.0
+    g_bad = 0
+    for s_r, b_r in parts:                       # rank order
+        g_sum += s_r
+        g_bad += int(b_r)
+    barrier()
+    opt.step_all(w16, g16, m, v)
+    st = opt.status()
+    ok = g_bad == 0 and st["last_overflow"] == 0 and st["opt_step"] == START_STEP
+    norm = np.float32(np.sqrt(g_sum))
+    norm_err = abs(st["last_norm"] - float(norm)) / float(norm)
+    sumsq_err = abs(st["last_sumsq"] - g_sum) / g_sum
+    ok = ok and norm_err <= 1e-5 and sumsq_err <= 1e-12
+    wins = _windows_of_shard(L, lo, hi)
+    elems = 0
+    for a, b in wins:
+        w = oracle.synth_f16(b - a, a, SEED, synth.STREAM_W, 0.02)
+        mm = oracle.synth_f32(b - a, a, SEED, synth.STREAM_M, 1e-4)
+        vv = oracle.synth_f32(b - a, a, SEED, synth.STREAM_V, 1e-3, square=True)
+        oracle.apply_f16(cfg, oracle.make_state(LOSS_SCALE, START_STEP - 1), w,
+                         np.ascontiguousarray(g_host[a - lo:b - lo]), mm, vv, a, g_sum, g_bad)
+        ok = ok and np.array_equal(g16[a - lo:b - lo].cpu().numpy().view(np.uint16),
+                                   g_host[a - lo:b - lo])     # same generator on both sides
+        ok = ok and np.array_equal(w16[a - lo:b - lo].cpu().numpy().view(np.uint16), w)
+        ok = ok and np.array_equal(m[a - lo:b - lo].cpu().numpy().view(np.uint32),
+                                   mm.view(np.uint32))
+        ok = ok and np.array_equal(v[a - lo:b - lo].cpu().numpy().view(np.uint32),
+                                   vv.view(np.uint32))
+        elems += b - a
+    # replicated state: every rank's 64-byte status identical
+    keys = sorted(st)
+    mine = torch.tensor([float(st[k]) for k in keys], dtype=torch.float64, device=dev)
+    if world > 1:
+        lo_t, hi_t = mine.clone(), mine.clone()
+        dist.all_reduce(lo_t, op=dist.ReduceOp.MIN)
+        dist.all_reduce(hi_t, op=dist.ReduceOp.MAX)
+        same = bool(torch.equal(lo_t, hi_t))
+        counts = torch.tensor([1.0 if ok else 0.0, float(len(wins)), float(elems)],
+                              dtype=torch.float64, device=dev)
+        okf = counts[:1].clone()
+        dist.all_reduce(okf, op=dist.ReduceOp.MIN)
+        dist.all_reduce(counts, op=dist.ReduceOp.SUM)
+        ok_all = bool(okf.item() == 1.0)
+        n_wins, n_elems = int(counts[1].item()), int(counts[2].item())
+    else:
+        same, ok_all, n_wins, n_elems = True, bool(ok), len(wins), elems
+    return {"ok": bool(ok_all and same), "windows": n_wins, "elements": n_elems,
+            "state_identical": same, "norm_rel_err": float(norm_err),
+            "sumsq_rel_err": float(sumsq_err),
+            "checker": "CPU oracle (oracle/ark_oracle.c) on every rank's shard after the timed "
+                       "regions; one fresh device step; windows bit for bit",
+            "leg_s": round(time.perf_counter() - t0, 2)}
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -404,7 +727,7 @@ def run_ours(args):
     # per-kernel split is timed in a second region of K steps right after,
     # with event-record nodes between the kernels.  A state below 4x the L2
     # is timed step by step instead, with the L2 flushed between steps.
-    flush = needs_flush(L.n, world)
+    flush = {"auto": needs_flush(L.n, world), "flush": True, "none": False}[args.l2]
     # flush: write 256 MiB (evicts the L2), then read another 256 MiB, so that
     # the dirty flush lines are written back before the step, not during it
     scratch = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=dev) if flush else None
@@ -473,20 +796,44 @@ def run_ours(args):
     e2e_steps = min(args.steps, 50)
 
     # ---- e2e: host grads -> device, step, status back, every step ----
+    # the pinned host buffer is first touched by this process bound to the
+    # GPU's NUMA node, so its pages sit on the node nearest the GPU
+    cpus = numa_local_cpus(local) if hasattr(os, "sched_setaffinity") else None
+    prev_aff = os.sched_getaffinity(0) if cpus else None
+    if cpus and (cpus & prev_aff):
+        os.sched_setaffinity(0, cpus & prev_aff)
     g_host = torch.empty(n, dtype=torch.float16, pin_memory=True)
     g_host.copy_(g16.cpu())
+    if prev_aff:
+        os.sched_setaffinity(0, prev_aff)
     barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    marks = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(e2e_steps)]
     e0.record(stream)
-    for _ in range(e2e_steps):
+    for k in range(e2e_steps):
+        marks[k][0].record(stream)
         opt.upload_grads(g16, g_host)
+        marks[k][1].record(stream)
         opt.step_all(w16, g16, m, v)
+        marks[k][2].record(stream)
         opt.status()
     e1.record(stream)
     torch.cuda.synchronize()
     barrier()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps)
+    e2e_h2d_ms = max_over_ranks(float(np.mean([a.elapsed_time(b) for a, b, _ in marks])))
+    e2e_step_ms = max_over_ranks(float(np.mean([b.elapsed_time(c) for _, b, c in marks])))
+    # the host->device ceiling: the same pinned copy alone, every rank at once
+    h2d_alone_ms = timed_loop(lambda: opt.upload_grads(g16, g_host), min(e2e_steps, 20), stream,
+                              barrier, max_over_ranks)
+    e2e_split = {"h2d_ms": round(e2e_h2d_ms, 4), "step_ms": round(e2e_step_ms, 4),
+                 "h2d_alone_ms": round(h2d_alone_ms, 4),
+                 "h2d_aggregate_gbs": round(2 * L.n / (e2e_h2d_ms * 1e-3) / 1e9, 1),
+                 "h2d_alone_aggregate_gbs": round(2 * L.n / (h2d_alone_ms * 1e-3) / 1e9, 1),
+                 "pinned_numa_local": bool(cpus and (cpus & (prev_aff or set()))),
+                 "note": "events around the upload and around the step of each e2e step; "
+                         "the rest of e2e ms is the status read-back and host latency"}
 
     # ---- roofline of the dominant kernel (pass 2) ----
     peak, peak_src = measured_peak()
@@ -497,7 +844,7 @@ def run_ours(args):
         p2 = float(np.mean(prof[:, 2]))
         p2_max = max_over_ranks(p2)
         achieved = PASS2_BYTES_PER_PARAM * n / (p2 * 1e-3) / 1e9
-        tpp = kernel_traffic_per_param("pass2_adamw_eko.md")
+        tpp = PASS2_DRAM_BYTES_PER_PARAM
         roof = {"kernel": "ark::pass2_kernel (fused unscale+clip+AdamW)", "bound": "hbm",
                 "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "peak_source": peak_src,
@@ -516,12 +863,22 @@ def run_ours(args):
             roof["pass1_kernel"] = "ark::pass1_reduce_kernel (reduce-scatter over NVLink + norm/flag)"
             roof["nvlink_bytes_in_per_gpu"] = 2 * n * (world - 1)
             roof["nvlink_gbs_in_per_gpu"] = round(2 * n * (world - 1) / (p1 * 1e-3) / 1e9, 1)
-            roof["nvlink_peer_copy_gbs_measured"] = 770.0
+            roof["nvlink_peer_copy_gbs_measured"] = NVLINK_PEER_COPY_GBS
     clk = clocks.summary()
     geom = opt.geometry()
 
     aux = measure_aux(opt, L, w16, g16, m, v, stream, args, max_over_ranks, barrier) \
         if args.aux else None
+    allgather = None
+    if world > 1 and not args.no_allgather:
+        allgather = measure_allgather(opt, L, w16, g16, m, v, stream, args, max_over_ranks,
+                                      barrier)
+    legacy = None
+    if world == 1 and not args.no_legacy and not args.params and args.workload == "eko":
+        legacy = measure_legacy(L, stream, args)
+    parity = None
+    if not args.no_parity:
+        parity = parity_leg(opt, L, w16, g16, m, v, heavy, world, rank, dev, barrier)
 
     cpu = None
     if (rank == 0 and world == 1 and not args.no_cpu_baseline and not args.params
@@ -548,18 +905,21 @@ def run_ours(args):
                                     "p2p stores from pass 1 (nccl if unmappable)"),
                        "l2": ("L2 flushed between steps (256 MiB written, then another "
                               "256 MiB read so the dirty lines are written back first; both "
-                              "outside the per-step events; state %.3f GB/GPU < 4 x 126 MB L2)"
+                              "outside the per-step events; state %.3f GB/GPU, mode %s)"
                               if flush else
-                              "inputs larger than L2 (state %.2f GB/GPU vs 126 MB L2); no flush")
-                             % (n * STATE_BYTES_PER_PARAM / 1e9),
+                              "no flush between steps (state %.2f GB/GPU vs 126 MB L2, mode %s)")
+                             % (n * STATE_BYTES_PER_PARAM / 1e9, args.l2),
                        "geometry": geom},
             "roofline": roof,
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_val, 2), "unit": "GB/s", "ms_per_step": round(e2e_ms, 3),
                     "h2d_bytes_per_step": 2 * L.n, "d2h_bytes_per_step": 64 * world,
-                    "steps": e2e_steps,
+                    "steps": e2e_steps, "split": e2e_split,
                     "path": "Optimizer.upload_grads (pinned host fp16 grads) + step_all + "
                             "status() per step, through the C ABI"},
+            "parity": parity,
+            "allgather": allgather,
+            "legacy": legacy,
             "step_stats": step_stats,
             "gpu_launches": 2 * args.steps,
             "aux": aux,
@@ -595,6 +955,15 @@ def main():
     ap.add_argument("--nccl-exchange", action="store_true",
                     help="N > 1: exchange the partials with NCCL instead of peer-to-peer stores")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-parity", action="store_true",
+                    help="skip the oracle parity leg after the timed regions")
+    ap.add_argument("--no-allgather", action="store_true",
+                    help="N > 1: skip timing the FP16 weight all-gather (NCCL and fused)")
+    ap.add_argument("--no-legacy", action="store_true",
+                    help="N = 1: skip timing the legacy per-tensor entry points")
+    ap.add_argument("--l2", choices=("auto", "flush", "none"), default="auto",
+                    help="L2 handling between timed steps: flush below 4x L2 of state (auto), "
+                         "always, or never")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -81,7 +81,8 @@ ARK_API void ark_quant_f32_to_f16(const float* src, uint16_t* dst, uint64_t n);
 ARK_API void ark_dequant_f16_to_f32(const uint16_t* src, float* dst, uint64_t n);
 
 /* No counterpart in the reference.  The same clip as ark_asm_grad_clip
- * (same kernels, same grid, same result), for callers that cannot allocate
+ * (same kernels, same grid, the ARK_COMPAT_CLIP_NEON_FOLD setting honoured:
+ * the same norm and grads bit for bit), for callers that cannot allocate
  * device memory: a process whose HBM is taken up front by its own pool
  * allocator, where a cudaMalloc of even a few KiB fails, and code paths
  * that must not stall other work on the device, which cudaFree does.
@@ -89,13 +90,18 @@ ARK_API void ark_dequant_f16_to_f32(const uint16_t* src, float* dst, uint64_t n)
  * calls no cudaMalloc, cudaFree or allocating routine.  Its scratch is a
  * static 16.5 KiB array in the library's device image (one per GPU that
  * loads the library, held until exit) with room for 2048 thread-block
- * partial sums; a launch that needs more is rejected with
- * ARK_E_UNSUPPORTED.  grads: device, scaled in place; norm_out: a device
- * float that receives the pre-clip norm; enqueued on cuda_stream (NULL:
- * the default stream), nothing is waited for.  The first call on a device
- * looks up the array's device address (cudaGetSymbolAddress); make that
- * first call before any stream capture.  All calls share the array:
- * calls that overlap on the GPU (other streams, other threads) race. */
+ * partial sums (a B200 launches at most 1184); a launch that needs more is
+ * rejected with ARK_E_UNSUPPORTED.  grads: device, scaled in place;
+ * norm_out: a device float that receives the pre-clip norm; enqueued on
+ * cuda_stream (NULL: the default stream), nothing is waited for.  The first
+ * call on a device looks up the array's device address
+ * (cudaGetSymbolAddress) and, under CUDA's default lazy module loading,
+ * loads the library's device code, which takes device memory: make that
+ * first call (or set CUDA_MODULE_LOADING=EAGER) before the caller's pool
+ * reserves the HBM, and before any stream capture.  The address is kept for
+ * the life of the process: a cudaDeviceReset after the first call is not
+ * supported.  All calls share the array: calls that overlap on the GPU
+ * (other streams, other threads) race. */
 ARK_API int ark_cuda_grad_clip_noalloc(float* grads, uint64_t n, float threshold,
                                        float* norm_out, void* cuda_stream);
 
@@ -235,8 +241,53 @@ ARK_API int ark_cuda_opt_step_reduce(ark_opt_state* st, uint16_t* w16, uint16_t*
  *    are, so w32_out must be initialised once (dequant) before the first
  *    step. */
 #define ARK_STEP_REDUCE 0x1u
+/* ARK_STEP_GATHER_WEIGHTS: the ZeRO-1 weight all-gather fused with the
+ * update.  Every step that updates the weights also stores the updated
+ * shard into every rank's full weight buffer (ark_cuda_opt_weight_buffer)
+ * at its global offset, with plain stores over NVLink from the update
+ * kernel itself; w16 may be this rank's slice of its own full buffer.  Not
+ * combined with w32_out (ARK_E_UNSUPPORTED).  cfg.shard_offset must be a
+ * multiple of 8.  Before a rank reads its full buffer (the forward), it
+ * calls ark_cuda_opt_weights_wait. */
+#define ARK_STEP_GATHER_WEIGHTS 0x2u
 ARK_API int ark_cuda_opt_step_ex(ark_opt_state* st, uint16_t* w16, uint16_t* g16, float* m,
                                  float* v, float* w32_out, uint32_t options);
+
+/* The full FP16 weight buffer of this rank for ARK_STEP_GATHER_WEIGHTS
+ * (n_full elements, all global indices, zeroed), with every rank's buffer
+ * mapped into every other rank (collective: every rank calls it; needs the
+ * peer-to-peer exchange slots when world_size > 1).  The consumer is the
+ * forward, which reads every weight tensor (objc/bridge.m:630-737 over the
+ * shared weight buffers of src/memory.rs:207-236).  The library owns the
+ * buffer until ark_cuda_opt_destroy. */
+ARK_API int ark_cuda_opt_weight_buffer(ark_opt_state* st, uint64_t n_full, uint16_t** w16_full);
+
+/* Enqueue on the state's stream a bounded wait until every rank's last
+ * ARK_STEP_GATHER_WEIGHTS step has stored its shard into this rank's full
+ * weight buffer; work enqueued after it on the stream reads the complete
+ * updated weights.  A wait that runs out leaves ARK_E_TIMEOUT in the state.
+ * No-op with world_size 1. */
+ARK_API int ark_cuda_opt_weights_wait(ark_opt_state* st);
+
+/* Replaces the logits-gradient block of train_step (src/training.rs:228-245):
+ * counts non-finite values of the unscaled FP32 logits gradients
+ * (bs x vocab, device, any alignment) and multiplies every element in place
+ * by the current device loss scale (x *= loss_scale).  Enqueued on the
+ * state's stream, nothing is waited for.  A non-finite value makes the next
+ * optimizer step on this state (on every rank) a skipped overflow step:
+ * backoff, skipped and consecutive-overflow counts and the early-stop
+ * check, no optimizer step -- the same transitions as the reference's
+ * early return at :231-237.  Call it once per iteration, before the
+ * backward and the step; on a rejected iteration the buffer's contents are
+ * unspecified (the reference discards them). */
+ARK_API int ark_cuda_opt_logits_check(ark_opt_state* st, float* logits_grad, uint64_t n);
+
+/* Zero this rank's full gradient buffer (ark_cuda_opt_grad_buffer) on the
+ * state's stream: ModelWeights::zero_all_grads (src/memory.rs:338-342),
+ * called before every backward (src/training.rs:248) for a backward that
+ * accumulates with +=.  Safe once the previous step was enqueued: no peer
+ * reads this rank's buffer after that step has completed. */
+ARK_API int ark_cuda_opt_zero_grads(ark_opt_state* st);
 
 /* Wait for the state's stream and copy the device state out.  Returns
  * ARK_E_EARLY_STOP once the early-stop condition holds (training.rs:298),

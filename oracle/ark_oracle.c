@@ -377,6 +377,21 @@ ORK_API void ork_reduce_f16(const uint16_t* const* srcs, int nranks, uint64_t n,
     }
 }
 
+/* The logits-gradient block of train_step (training.rs:228-245): the finite
+ * check over the unscaled logits gradients (:229-230); if any value is
+ * non-finite the step is rejected before scaling (:231-237: the caller
+ * applies the overflow transitions, the same as ork_apply_f16's overflow
+ * branch), else every value is multiplied by the loss scale (:244-245,
+ * `*x *= self.loss_scale`, one f32 multiply).  Returns the number of
+ * non-finite values. */
+ORK_API uint64_t ork_logits_check_scale(float* x, uint64_t n, float loss_scale) {
+    uint64_t bad = 0;
+    for (uint64_t i = 0; i < n; ++i) bad += !isfinite(x[i]);
+    if (bad) return bad;
+    for (uint64_t i = 0; i < n; ++i) x[i] = x[i] * loss_scale;
+    return 0;
+}
+
 /* Warmup + cosine schedule, optimizer.rs:80-92, in f32 (cosf from libm). */
 ORK_API float ork_lr_now(float lr, uint32_t warmup, uint32_t step) {
     if (step < warmup) return lr * ((float)step + 1.0f) / (float)warmup;
@@ -471,6 +486,16 @@ ORK_API int ork_ref_step_tensors(ork_tensor* ts, int nt, ork_amp_state* st,
     }
     st->last_overflow = 0; st->last_norm = norm;
     return 0;
+}
+
+/* Host threads of the oracle's parallel loops from now on (checker legs
+ * running in several processes at once split the cores between them). */
+ORK_API void ork_set_threads(int threads) {
+#ifdef _OPENMP
+    if (threads > 0) omp_set_num_threads(threads);
+#else
+    (void)threads;
+#endif
 }
 
 ORK_API int ork_max_threads(void) {

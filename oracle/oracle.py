@@ -78,11 +78,13 @@ def lib():
             "ork_ref_step_tensors": (c_i, [ctypes.POINTER(Tensor), c_i, ctypes.POINTER(AmpState), c_f,
                                            c_f, c_f, c_f, c_f, c_f, c_u32, c_i]),
             "ork_max_threads": (c_i, []),
+            "ork_set_threads": (None, [c_i]),
             "ork_splitmix64": (c_u64, [c_u64]),
             "ork_normal": (c_f, [c_u64, c_u64, c_u64]),
             "ork_synth_f16": (None, [c_p, c_u64, c_u64, c_u64, c_u64, c_f, c_f, c_u32, c_f]),
             "ork_synth_f32": (None, [c_p, c_u64, c_u64, c_u64, c_u64, c_f, c_i]),
             "ork_inject_index": (c_u64, [c_u64, c_u32, c_u64]),
+            "ork_logits_check_scale": (c_u64, [c_p, c_u64, c_f]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)
@@ -186,6 +188,14 @@ def reduce_f16(srcs, n, offset):
     out = np.empty(n, np.uint16)
     lib().ork_reduce_f16(arr, len(srcs), n, offset, ptr(out))
     return out
+
+
+def logits_check_scale(x, loss_scale):
+    """training.rs:228-245 on a copy: (non-finite count, logits after the
+    block -- scaled when every value is finite, else unchanged)."""
+    x = np.array(x, np.float32, copy=True)
+    bad = lib().ork_logits_check_scale(ptr(x), len(x), loss_scale)
+    return int(bad), x
 
 
 def synth_f16(n, offset, seed, stream, sigma, mult=1.0, heavy_every=0, heavy_mult=1.0):

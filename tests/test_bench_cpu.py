@@ -27,3 +27,23 @@ def test_bounded_reference_step_takes_a_prefix(oracle):
     assert step.n_tensors == 1 and step.n_params == L.tensors[0].numel
     full, _ = bench.bounded_reference_step(L, 2, 1, budget_s=60.0)
     assert full.n_tensors == L.n_tensors
+
+
+def test_parity_windows_cover_each_shard_boundary():
+    """The parity leg's windows lie inside the rank's shard and include its
+    two ends and every weight-decay / tensor boundary inside it."""
+    L = layout.eko_layout()
+    for world in (1, 2, 8):
+        for r in range(world):
+            lo, hi = L.shard(r, world)
+            wins = bench._windows_of_shard(L, lo, hi)
+            assert wins and all(lo <= a < b <= hi for a, b in wins)
+            assert any(a == lo for a, _ in wins) and any(b == hi for _, b in wins)
+            bounds = [L.n_decay] + [L.offsets[t.name] for t in L.flat]
+            for x in bounds:
+                if lo + 1024 <= x <= hi - 1024:
+                    assert any(a < x < b for a, b in wins), (world, r, x)
+
+
+def test_numa_lookup_tolerates_missing_sysfs():
+    assert bench.numa_local_cpus(0) is None or isinstance(bench.numa_local_cpus(0), set)

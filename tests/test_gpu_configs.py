@@ -64,8 +64,9 @@ def _full_size_check(oracle, L, heavy, extra_windows=()):
     for (lo, hi), (w0, m0, v0) in pre.items():
         ow, om, ov = w0.copy(), m0.copy(), v0.copy()
         wst = oracle.make_state(SCALE, opt_step=999)
+        # the oracle's own exact sum drives the clip coefficient of the windows
         oracle.apply_f16(cfg, wst, ow, np.ascontiguousarray(g_host[lo:hi]), om, ov, lo,
-                         st["last_sumsq"], 0)
+                         sumsq, 0)
         assert same_f16(w16[lo:hi].cpu().numpy().view(np.uint16), ow), (lo, hi)
         assert same_f32(m[lo:hi].cpu().numpy(), om), (lo, hi)
         assert same_f32(v[lo:hi].cpu().numpy(), ov), (lo, hi)

@@ -277,3 +277,198 @@ def test_reduce_scatter_step_matches_oracle(oracle, world):
         assert np.array_equal(ws, w[lo:hi]), rank
         assert np.array_equal(ms.view(np.uint32), m[lo:hi].view(np.uint32)), rank
         assert np.array_equal(vs.view(np.uint32), v[lo:hi].view(np.uint32)), rank
+
+
+def _gather_rank_main(rank, world, port, q):
+    import datetime
+
+    import torch.distributed as dist
+
+    import ark_b200 as ab
+    from ark_b200 import dist as adist
+    from ark_b200 import layout, synth
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+    comm = adist.nccl_comm(rank, world, rank)
+    try:
+        L = layout.decoder_layout("multi", 4, 96, 256, 1000)
+        adam = ab.AdamConfig(lr=3e-4, beta1=0.9, beta2=0.95, eps=1e-8, weight_decay=0.1,
+                             grad_clip=1.0)
+        sc = ab.LossScaleConfig(init=2048.0, every=2, max=2.0 ** 24)
+        opt = ab.Optimizer(L, adam, sc, device=rank, rank=rank, world=world, comm=comm,
+                           constant_lr=True, initial_step=99, use_graph=True)
+        lo, hi, n = opt.lo, opt.hi, opt.n
+        full = opt.weight_buffer()
+        _, g16, m, v = synth.make_state(n, lo, 33, "cuda", loss_scale=2048.0)
+        w16 = full[lo:hi]                              # the shard lives in the full buffer
+        synth.fill_f16(w16, lo, 33, synth.STREAM_W, 0.02)
+        logits = torch.empty(4099, dtype=torch.float32, device="cuda")
+        statuses, fulls = [], []
+        for k in range(1, 6):
+            synth.fill_f32(logits, 0, 33, 0x900 + 16 * k + rank, 1e-2)
+            if k == 2 and rank == world - 1:
+                logits[17] = float("nan")              # one rank's logits are bad
+            opt.logits_check(logits)
+            synth.fill_grads(g16, lo, 33 + k, opt.status()["loss_scale"])
+            opt.step_gather(w16, g16, m, v)
+            opt.weights_wait()
+            statuses.append(opt.status())
+            fulls.append(full.cpu().numpy().view(np.uint16).copy())
+        q.put((rank, lo, hi, statuses, fulls, m.cpu().numpy(), v.cpu().numpy()))
+        opt.close()
+    finally:
+        adist.nccl_comm_destroy(comm)
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason="needs 2 GPUs")
+@pytest.mark.parametrize("world", WORLDS)
+def test_fused_weight_gather_and_logits_check_match_oracle(oracle, world):
+    """Every rank's full weight buffer equals the oracle's whole-buffer
+    weights after every step (the shard stored by the update kernel into
+    every peer over NVLink); one rank's non-finite logits skip the step on
+    every rank."""
+    from ark_b200 import layout, synth
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_gather_rank_main, args=(r, world, port, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    res = sorted([q.get(timeout=300) for _ in range(world)], key=lambda r: r[0])
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    L = layout.decoder_layout("multi", 4, 96, 256, 1000)
+    n = L.n
+    w = oracle.synth_f16(n, 0, 33, synth.STREAM_W, 0.02)
+    m = oracle.synth_f32(n, 0, 33, synth.STREAM_M, 1e-4)
+    v = oracle.synth_f32(n, 0, 33, synth.STREAM_V, 1e-3, square=True)
+    cfg = oracle.make_cfg(n_decay=L.n_decay, scale_every=2, scale_max=2.0 ** 24)
+    st = oracle.make_state(2048.0, opt_step=99)
+    ref_w, ref_st = [], []
+    for k in range(1, 6):
+        g = oracle.synth_f16(n, 0, 33 + k, synth.STREAM_G, 1e-3, st.loss_scale)
+        if k == 2:
+            oracle.apply_f16(cfg, st, w, g, m, v, 0, 0.0, 1)    # rejected at the logits check
+        else:
+            s, bad = oracle.partial_f16(cfg, st, g, 0)
+            oracle.apply_f16(cfg, st, w, g, m, v, 0, s, bad)
+        ref_w.append(w.copy())
+        ref_st.append((st.loss_scale, st.opt_step, st.last_overflow, st.clean_steps))
+    for rank, lo, hi, sts, fulls, ms, vs in res:
+        for k in range(5):
+            assert np.array_equal(fulls[k], ref_w[k]), (rank, k)
+            s = sts[k]
+            assert (s["loss_scale"], s["opt_step"], s["last_overflow"], s["clean_steps"]) == \
+                ref_st[k], (rank, k, s)
+        assert np.array_equal(ms.view(np.uint32), m[lo:hi].view(np.uint32)), rank
+        assert np.array_equal(vs.view(np.uint32), v[lo:hi].view(np.uint32)), rank
+
+
+def _windows_of_shard(L, lo, hi, span=2048):
+    """Windows of [lo, hi): the shard ends, the weight-decay boundary and
+    tensor boundaries that fall inside it."""
+    cand = [lo, hi - span, (lo + hi) // 2, L.n_decay - span // 2]
+    cand += [L.offsets[t.name] - span // 2 for t in L.flat]
+    out = set()
+    for a in cand:
+        a = max(lo, min(a, hi - span))
+        if lo <= a < hi:
+            out.add((a, min(a + span, hi)))
+    return sorted(out)
+
+
+def _big_rank_main(rank, world, port, q, workload):
+    import datetime
+
+    os.environ["OMP_NUM_THREADS"] = str(max(1, (os.cpu_count() or 8) // world))
+    import torch.distributed as dist
+
+    import ark_b200 as ab
+    from ark_b200 import dist as adist
+    from ark_b200 import layout, synth
+    from oracle import oracle
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=300))
+    comm = adist.nccl_comm(rank, world, rank)
+    try:
+        L = layout.LAYOUTS[workload]()
+        heavy = workload == "7b"
+        adam = ab.AdamConfig(lr=3e-4, beta1=0.9, beta2=0.95, eps=1e-8, weight_decay=0.1,
+                             grad_clip=1.0)
+        sc = ab.LossScaleConfig(init=65536.0, every=2000, max=2.0 ** 24)
+        opt = ab.Optimizer(L, adam, sc, device=rank, rank=rank, world=world, comm=comm,
+                           constant_lr=True, initial_step=999)
+        lo, hi, n = opt.lo, opt.hi, opt.n
+        w16, g16, m, v = synth.make_state(n, lo, 4242, "cuda", loss_scale=65536.0, heavy=heavy)
+        opt.step_all(w16, g16, m, v)
+        st = opt.status()
+        wins = _windows_of_shard(L, lo, hi)
+        got = [(a, b, w16[a - lo:b - lo].cpu().numpy().view(np.uint16).copy(),
+                m[a - lo:b - lo].cpu().numpy().copy(), v[a - lo:b - lo].cpu().numpy().copy())
+               for a, b in wins]
+        g_host = oracle.synth_f16(n, lo, 4242, synth.STREAM_G, 1e-3, 65536.0,
+                                  synth.HEAVY_EVERY if heavy else 0,
+                                  synth.HEAVY_MULT if heavy else 1.0)
+        cfg = oracle.make_cfg(n_decay=L.n_decay, scale_every=2000, scale_max=2.0 ** 24)
+        sumsq, bad = oracle.partial_f16(cfg, oracle.make_state(65536.0, 999), g_host, lo)
+        gwin = [np.ascontiguousarray(g_host[a - lo:b - lo]) for a, b in wins]
+        q.put((rank, lo, hi, sumsq, bad, st, got, gwin))
+        opt.close()
+    finally:
+        adist.nccl_comm_destroy(comm)
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 8, reason="needs 8 GPUs")
+def test_7b_sharded_over_8_windows_match_oracle(oracle):
+    """BASELINE's 7B configuration (heavy-tailed gradients, clipping active)
+    ZeRO-1 sharded over 8 B200: every rank's windows (shard ends, the
+    weight-decay boundary, tensor boundaries) bit for bit against the
+    oracle driven by the oracle's own global sum of squares, and the
+    replicated state identical on every rank."""
+    from ark_b200 import layout, synth
+    world = 8
+    port = _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_big_rank_main, args=(r, world, port, q, "7b"))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    res = sorted([q.get(timeout=900) for _ in range(world)], key=lambda r: r[0])
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    L = layout.LAYOUTS["7b"]()
+    sumsq = 0.0
+    for r in res:                                     # rank order
+        sumsq += r[3]
+        assert r[4] == 0
+    cfg = oracle.make_cfg(n_decay=L.n_decay, scale_every=2000, scale_max=2.0 ** 24)
+    norm = np.float32(np.sqrt(sumsq))
+    sts = [r[5] for r in res]
+    assert all(s == sts[0] for s in sts)              # replicated state identical
+    assert abs(sts[0]["last_sumsq"] - sumsq) <= 1e-12 * sumsq
+    assert abs(sts[0]["last_norm"] - norm) <= 1e-5 * norm
+    assert sts[0]["last_clip_coef"] < 0.01 and sts[0]["opt_step"] == 1000
+    for rank, lo, hi, _, _, _, got, gwin in res:
+        for (a, b, dw, dm, dv), g in zip(got, gwin):
+            w = oracle.synth_f16(b - a, a, 4242, synth.STREAM_W, 0.02)
+            m = oracle.synth_f32(b - a, a, 4242, synth.STREAM_M, 1e-4)
+            v = oracle.synth_f32(b - a, a, 4242, synth.STREAM_V, 1e-3, square=True)
+            ost = oracle.make_state(65536.0, opt_step=999)
+            oracle.apply_f16(cfg, ost, w, g, m, v, a, sumsq, 0)
+            assert np.array_equal(dw, w), (rank, a)
+            assert np.array_equal(dm.view(np.uint32), m.view(np.uint32)), (rank, a)
+            assert np.array_equal(dv.view(np.uint32), v.view(np.uint32)), (rank, a)
