@@ -21,6 +21,7 @@
 
 #include "ark_device.cuh"
 #include "ark_internal.h"
+#include "ark_sync.cuh"
 
 namespace ark {
 
@@ -360,6 +361,7 @@ __global__ void __launch_bounds__(kT) clip_norm_kernel(const float* __restrict__
                                                       float thr, ClipScratch sc) {
     __shared__ double s_sum[kT / 32];
     __shared__ int s_last;
+    griddep_launch_dependents();   // the scale kernel may start loading g
     double acc = 0.0, acc1 = 0.0;
     const uint64_t stride = (uint64_t)gridDim.x * kT;
     if (aligned16(g)) {
@@ -434,31 +436,44 @@ __global__ void clip_neon_fold_kernel(const float* __restrict__ g, uint64_t n, f
     }
 }
 
+// The scale pass, launched as a programmatic dependent of the norm kernel
+// (or the compat fold kernel): its blocks start as the norm kernel's retire,
+// load their first round of g (which the norm pass only reads), then wait
+// for the norm pass's result.  It walks g in reverse so that the first
+// lines it touches are the last ones the norm pass read, still in L2.
 __global__ void __launch_bounds__(kT) clip_scale_kernel(float* __restrict__ g, uint64_t n,
                                                        const ClipResult* __restrict__ res) {
-    if (!res->apply) return;
-    const float s = res->scale;
     const uint64_t stride = (uint64_t)gridDim.x * kT;
     if (aligned16(g)) {
         const uint64_t nq = n >> 2;
         float4* g4 = reinterpret_cast<float4*>(g);
-        for (uint64_t base = (uint64_t)blockIdx.x * kT + threadIdx.x; base < nq;
-             base += stride * kClipU) {
-            float4 x[kClipU];
+        uint64_t base = (uint64_t)blockIdx.x * kT + threadIdx.x;
+        float4 x[kClipU];
+#pragma unroll
+        for (int u = 0; u < kClipU; ++u) {
+            const uint64_t j = base + u * stride;
+            if (j < nq) x[u] = ld_stream(g4 + (nq - 1 - j));
+        }
+        griddep_wait();
+        if (!res->apply) return;
+        const float s = res->scale;
+        while (base < nq) {
 #pragma unroll
             for (int u = 0; u < kClipU; ++u) {
-                const uint64_t i = base + u * stride;
-                if (i < nq) x[u] = ld_stream(g4 + i);
-            }
-#pragma unroll
-            for (int u = 0; u < kClipU; ++u) {
-                const uint64_t i = base + u * stride;
-                if (i >= nq) continue;
+                const uint64_t j = base + u * stride;
+                if (j >= nq) continue;
                 x[u].x = __fmul_rn(x[u].x, s);
                 x[u].y = __fmul_rn(x[u].y, s);
                 x[u].z = __fmul_rn(x[u].z, s);
                 x[u].w = __fmul_rn(x[u].w, s);
-                st_stream(g4 + i, x[u]);
+                st_stream(g4 + (nq - 1 - j), x[u]);
+            }
+            base += stride * kClipU;
+            if (base >= nq) break;
+#pragma unroll
+            for (int u = 0; u < kClipU; ++u) {
+                const uint64_t j = base + u * stride;
+                if (j < nq) x[u] = ld_stream(g4 + (nq - 1 - j));
             }
         }
         if (blockIdx.x == 0 && threadIdx.x < (n & 3u)) {
@@ -466,9 +481,27 @@ __global__ void __launch_bounds__(kT) clip_scale_kernel(float* __restrict__ g, u
             g[i] = __fmul_rn(g[i], s);
         }
     } else {
+        griddep_wait();
+        if (!res->apply) return;
+        const float s = res->scale;
         for (uint64_t i = (uint64_t)blockIdx.x * kT + threadIdx.x; i < n; i += stride)
             g[i] = __fmul_rn(g[i], s);
     }
+}
+
+// The scale pass as a programmatic dependent of the kernel before it.
+static cudaError_t launch_clip_scale(int blocks, cudaStream_t s, float* g, uint64_t n,
+                                     const ClipResult* res) {
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cudaLaunchConfig_t lc = {};
+    lc.gridDim = dim3((unsigned)blocks);
+    lc.blockDim = dim3(kT);
+    lc.stream = s;
+    lc.attrs = attr;
+    lc.numAttrs = 1;
+    return cudaLaunchKernelEx(&lc, clip_scale_kernel, g, n, res);
 }
 
 // Grids of the two clip kernels (norm, scale) for n elements: one
@@ -518,7 +551,7 @@ static int clip_launch(float* g, uint64_t n, float thr, float* norm_out) {
         clip_neon_fold_kernel<<<1, 32, 0, s>>>(g, n, thr, sc.res);
     else
         clip_norm_kernel<<<blocks, kT, 0, s>>>(g, n, thr, sc);
-    clip_scale_kernel<<<sblocks, kT, 0, s>>>(g, n, sc.res);
+    if (launch_clip_scale(sblocks, s, g, n, sc.res) != cudaSuccess) return ARK_E_CUDA;
     if (cudaGetLastError() != cudaSuccess) return ARK_E_CUDA;
     ClipResult r;
     // the norm is the return value: this entry point always waits
@@ -591,7 +624,7 @@ static int clip_noalloc_launch(float* g, uint64_t n, float thr, float* norm_dev,
             return ARK_E_CUDA;
         clip_norm_kernel<<<blocks, kT, 0, s>>>(g, n, thr, sc);
     }
-    clip_scale_kernel<<<sblocks, kT, 0, s>>>(g, n, sc.res);
+    if (launch_clip_scale(sblocks, s, g, n, sc.res) != cudaSuccess) return ARK_E_CUDA;
     if (cudaGetLastError() != cudaSuccess) return ARK_E_CUDA;
     if (cudaMemcpyAsync(norm_dev, &sc.res->norm, sizeof(float), cudaMemcpyDeviceToDevice, s) !=
         cudaSuccess)
