@@ -87,6 +87,21 @@ static uint64_t resident_capacity(const void* kernel, int threads, size_t dyn_sm
     return full;
 }
 
+// SMs of the current device (looked up once per device).
+static int sm_count() {
+    static std::atomic<int> cache[64];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64) dev = 0;
+    int v = cache[dev].load();
+    if (v <= 0) {
+        v = 148;
+        cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+        cache[dev].store(v);
+    }
+    return v;
+}
+
 int streaming_grid(const void* kernel, int threads, size_t dyn_smem, uint64_t work_items) {
     const uint64_t full = resident_capacity(kernel, threads, dyn_smem);
     uint64_t need = (work_items + threads - 1) / threads;
@@ -441,8 +456,12 @@ __global__ void clip_neon_fold_kernel(const float* __restrict__ g, uint64_t n, f
 // load their first round of g (which the norm pass only reads), then wait
 // for the norm pass's result.  It walks g in reverse so that the first
 // lines it touches are the last ones the norm pass read, still in L2.
+// `res` is written by the kernel this one overlaps: it is read only after
+// griddep_wait, through a volatile pointer (a const __restrict__ pointer
+// would let the compiler treat it as unchanging and load it early).
 __global__ void __launch_bounds__(kT) clip_scale_kernel(float* __restrict__ g, uint64_t n,
-                                                       const ClipResult* __restrict__ res) {
+                                                       const ClipResult* res_ptr) {
+    const volatile ClipResult* res = res_ptr;
     const uint64_t stride = (uint64_t)gridDim.x * kT;
     if (aligned16(g)) {
         const uint64_t nq = n >> 2;
@@ -633,7 +652,13 @@ static int clip_noalloc_launch(float* g, uint64_t n, float thr, float* norm_dev,
 }
 
 // ------------------------------------------------------------ conversions
-constexpr int kConvU = 2;   // 8-element vectors in flight per thread
+constexpr int kConvU = 2;   // quant: 8-element vectors in flight per thread
+// dequant (2 B read, 4 B written per element): one vector per thread per
+// iteration at 5 blocks of 256 per SM measured fastest on B200 (2^27
+// elements: 6.24 TB/s; 2 in flight at 4 blocks/SM 4.80, at 3 blocks/SM 6.21;
+// one at 4 or 6 blocks/SM 5.85 / 4.83)
+constexpr int kDeqU = 1;
+constexpr int kDeqBlocksPerSM = 5;
 __global__ void __launch_bounds__(kT) quant_kernel(const float* __restrict__ src,
                                                   uint16_t* __restrict__ dst, uint64_t n, int vec) {
     const uint64_t stride = (uint64_t)gridDim.x * kT;
@@ -680,15 +705,15 @@ __global__ void __launch_bounds__(kT) dequant_kernel(const uint16_t* __restrict_
         const uint4* s4 = reinterpret_cast<const uint4*>(src);
         float4* d4 = reinterpret_cast<float4*>(dst);
         for (uint64_t base = (uint64_t)blockIdx.x * kT + threadIdx.x; base < n8;
-             base += stride * kConvU) {
-            uint4 q[kConvU];
+             base += stride * kDeqU) {
+            uint4 q[kDeqU];
 #pragma unroll
-            for (int u = 0; u < kConvU; ++u) {
+            for (int u = 0; u < kDeqU; ++u) {
                 const uint64_t i = base + u * stride;
                 if (i < n8) q[u] = ld_stream(s4 + i);
             }
 #pragma unroll
-            for (int u = 0; u < kConvU; ++u) {
+            for (int u = 0; u < kDeqU; ++u) {
                 const uint64_t i = base + u * stride;
                 if (i >= n8) continue;
                 st_stream(d4 + 2 * i, make_float4(h2f(lo16(q[u].x)), h2f(hi16(q[u].x)),
@@ -717,8 +742,10 @@ static int convert_launch(const void* src, void* dst, uint64_t n, bool quant) {
         quant_kernel<<<blocks, kT, 0, s>>>(static_cast<const float*>(src),
                                             static_cast<uint16_t*>(dst), n, vec);
     } else {
-        const int blocks = streaming_grid(reinterpret_cast<const void*>(dequant_kernel), kT, 0,
-                                          vec ? (n >> 3) / kConvU + 1 : n);
+        int blocks = streaming_grid(reinterpret_cast<const void*>(dequant_kernel), kT, 0,
+                                    vec ? (n >> 3) / kDeqU + 1 : n);
+        const int cap = sm_count() * kDeqBlocksPerSM;
+        if (blocks > cap) blocks = cap;
         dequant_kernel<<<blocks, kT, 0, s>>>(static_cast<const uint16_t*>(src),
                                               static_cast<float*>(dst), n, vec);
     }

@@ -70,6 +70,8 @@ struct StepParams {
     unsigned long long* blk_bad;
     unsigned int* ticket1;
     unsigned int* ticket2;
+    int p1_last;                     // pass 1's last block forms the rank partial (NCCL exchange)
+    unsigned int nblk1;              // pass-1 blocks (partials pass 2 reduces otherwise)
     Partial* part_local;             // this rank's partial (NCCL all-gather send buffer)
     Partial* part_all;               // [world] partials of every rank, rank order
     uint64_t* xchg;                  // own receive slots [2][world] x kSlotWords (slot_of)
@@ -161,22 +163,19 @@ __device__ __forceinline__ uint64_t* slot_of(uint64_t* base, unsigned long long 
                    kSlotWords);
 }
 
-// Last pass-1 block, world > 1 over mapped peer slots: lane r (< world) of
+// Pass 2, block 0, world > 1 over mapped peer slots: lane r (< world) of
 // warp 0 stores this rank's partial into rank r's slot [epoch & 1][rank]
-// (payload, then the epoch with release semantics) and returns: pass 1
-// never waits for a peer.  The wait is in pass 2 (gather_partials_p2p),
-// where it overlaps the first round of loads.  Slots alternate with the
-// epoch parity: a rank publishes epoch e + 2 into the slot of epoch e only
-// after its pass 2 of step e + 1 has seen every rank's partial e + 1, which
-// every rank publishes only after its own pass 2 of step e (the last reader
-// of epoch e) has completed.
-__device__ void publish_partial_p2p(const StepParams& p, double my_sum,
-                                    unsigned long long my_bad) {
+// (payload, then the epoch with release semantics).  Slots alternate with
+// the epoch parity: a rank publishes epoch e + 2 into the slot of epoch e
+// only after its pass 2 of step e + 1 has seen every rank's partial e + 1,
+// which every rank publishes only after its own pass 2 of step e (the last
+// reader of epoch e) has completed.
+__device__ void publish_partial_p2p(const StepParams& p, unsigned long long epoch,
+                                    const Partial& mine) {
     const int r = threadIdx.x;
-    if (r >= p.world) return;
-    const unsigned long long epoch = p.st->steps_called + 1ull;
+    if (r >= p.world || r == p.rank) return;
     uint64_t* dst = slot_of(p.peers[r], epoch, p.world, p.rank);
-    st_relaxed_sys_v2(dst + kSlotSum, (uint64_t)__double_as_longlong(my_sum), my_bad);
+    st_relaxed_sys_v2(dst + kSlotSum, (uint64_t)__double_as_longlong(mine.sumsq), mine.nonfinite);
     st_release_sys(dst + kSlotEpoch, epoch);
 }
 
@@ -196,30 +195,32 @@ __device__ bool wait_partial(const StepParams& p, unsigned long long epoch, int 
     return true;
 }
 
-// Pass 2, every block, warp 0: this step's partial of every rank from this
-// rank's receive slots into out[0, world) (shared memory).  The outcome is
-// made uniform across the grid's blocks: the first block to decide (every
+// Pass 2, every block, warp 0: every rank's partial of this step into
+// out[0, world) (shared memory); out[rank] is this rank's own partial, which
+// every block has reduced itself, so only the peers' are waited for (in this
+// rank's receive slots, bounded by the global timer).  The outcome is made
+// uniform across the grid's blocks: the first block to decide (every
 // partial arrived, or a wait ran out) records (epoch << 1 | ok) in
 // p.verdict with a compare-and-swap and every block follows it, so no block
 // updates while another skips.  A block that timed out while the verdict
-// says every partial arrived reads them again (they are in this GPU's
-// memory by then); if even that wait runs out it marks its partials as
-// missing (its vectors are not updated) and the state reports
-// ARK_E_TIMEOUT.  Returns in lane 0 of warp 0.
-__device__ void gather_partials_p2p(const StepParams& p, Partial* out) {
+// says every partial arrived reads them again (they are in this GPU's memory
+// by then); if even that wait runs out it marks its partials as missing (its
+// vectors are not updated) and the state reports ARK_E_TIMEOUT.
+__device__ void gather_partials_p2p(const StepParams& p, unsigned long long epoch,
+                                    const Partial& mine, Partial* out) {
     const int lane = threadIdx.x;
-    const unsigned long long epoch = p.st->steps_called + 1ull;
     bool ok = true;
-    if (lane < p.world) ok = wait_partial(p, epoch, lane, &out[lane]);
+    if (lane == p.rank) out[lane] = mine;
+    else if (lane < p.world) ok = wait_partial(p, epoch, lane, &out[lane]);
     const bool all_ok = __all_sync(0xFFFFFFFFu, ok);
     unsigned long long v = 0;
     if (lane == 0) {
-        const unsigned long long mine = (epoch << 1) | (all_ok ? 1ull : 0ull);
+        const unsigned long long want = (epoch << 1) | (all_ok ? 1ull : 0ull);
         v = *reinterpret_cast<volatile unsigned long long*>(p.verdict);
         while ((v >> 1) != epoch) {
-            const unsigned long long w = atomicCAS(p.verdict, v, mine);
+            const unsigned long long w = atomicCAS(p.verdict, v, want);
             if (w == v) {
-                v = mine;
+                v = want;
                 break;
             }
             v = w;
@@ -227,7 +228,7 @@ __device__ void gather_partials_p2p(const StepParams& p, Partial* out) {
     }
     v = __shfl_sync(0xFFFFFFFFu, v, 0);
     const bool verdict_ok = (v & 1ull) != 0;
-    if (verdict_ok && !all_ok && lane < p.world && !ok) ok = wait_partial(p, epoch, lane, &out[lane]);
+    if (verdict_ok && !ok && lane < p.world) ok = wait_partial(p, epoch, lane, &out[lane]);
     if (lane < p.world && (!verdict_ok || !ok)) {
         out[lane].sumsq = 0.0;
         out[lane].nonfinite = kPartialTimeout;
@@ -292,8 +293,38 @@ __device__ __forceinline__ void p1_consume1(P1Acc& a, uint16_t h, uint64_t i, co
     }
 }
 
-// Block reduction, last-block fixed-order reduction and the rank exchange.
-// `failed` (any thread) marks this rank's partial as unusable.
+// A block whose partial is unusable (its gradients-ready wait ran out) adds
+// kFailBit to the block's non-finite count; real counts stay below 2^40.
+constexpr unsigned long long kFailBit = 1ull << 40;
+
+// Fixed-order reduction of pass 1's per-block partials into this rank's
+// partial (valid in thread 0; every thread of the block must call it).  The
+// same code in every block gives the same value bit for bit, so pass 2 runs
+// it in every block instead of a last pass-1 block running it once.
+__device__ Partial reduce_block_partials(const StepParams& p, unsigned int nblk) {
+    __shared__ double s_sum[kThreads / 32];
+    __shared__ unsigned long long s_bad[kThreads / 32];
+    double s = 0.0;
+    unsigned long long b = 0;
+    for (unsigned int i = threadIdx.x; i < nblk; i += kThreads) {
+        s += __ldcg(p.blk_sum + i);
+        const unsigned long long x = __ldcg(p.blk_bad + i);
+        b += x == kPartialTimeout ? kFailBit : x;
+    }
+    s = block_sum<kThreads>(s, s_sum);
+    b = block_sum_u64<kThreads>(b, s_bad);
+    Partial r;
+    r.sumsq = s;
+    r.nonfinite = b >= kFailBit ? kPartialTimeout : b;   // threads that saw an inf/NaN
+    return r;
+}
+
+// End of pass 1 in every block: the block's sum of squares and non-finite
+// count (`failed` in any thread marks the block's partial unusable).  With
+// p.p1_last (the NCCL exchange between the kernels) the last block to
+// finish also reduces the block partials into this rank's partial, folds in
+// the logits count and writes it for the all-gather; otherwise pass 2 does
+// that reduction and pass 1 retires here.
 __device__ void p1_finish(const P1Acc& a, const P1Scale& sc, bool failed, const StepParams& p) {
     __shared__ double s_sum[kThreads / 32];
     __shared__ unsigned long long s_bad[kThreads / 32];
@@ -304,47 +335,27 @@ __device__ void p1_finish(const P1Acc& a, const P1Scale& sc, bool failed, const 
     const double acc = sc.pow2 ? __fma_rn(acc_s, inv_d * inv_d, a.acc_k) : acc_s;
     const bool raw_nonfinite = sc.pow2 && !isfinite(acc_s + a.acc_k);
     const unsigned long long bad =
-        raw_nonfinite || ((a.amax & 0xFFFFu) >= 0x7C00u) || ((a.amax >> 16) >= 0x7C00u);
+        (raw_nonfinite || ((a.amax & 0xFFFFu) >= 0x7C00u) || ((a.amax >> 16) >= 0x7C00u) ? 1ull
+                                                                                       : 0ull) +
+        (failed ? kFailBit : 0ull);
     const double bsum = block_sum<kThreads>(acc, s_sum);
     const unsigned long long bbad = block_sum_u64<kThreads>(bad, s_bad);
-    const unsigned long long bfail = block_sum_u64<kThreads>(failed ? 1ull : 0ull, s_bad);
     if (threadIdx.x == 0) {
         p.blk_sum[blockIdx.x] = bsum;
-        p.blk_bad[blockIdx.x] = bfail ? kPartialTimeout : bbad;
+        p.blk_bad[blockIdx.x] = bbad >= kFailBit ? kPartialTimeout : bbad;
     }
+    if (!p.p1_last) return;
     if (!last_block_arrived(p.ticket1, &s_last)) return;
-    // Last block: fixed-order reduction of the per-block partials.
-    double s = 0.0;
-    unsigned long long b = 0, f = 0;
-    for (unsigned int i = threadIdx.x; i < gridDim.x; i += kThreads) {
-        s += __ldcg(p.blk_sum + i);
-        const unsigned long long x = __ldcg(p.blk_bad + i);
-        if (x == kPartialTimeout) f = 1;
-        else b += x;
-    }
-    s = block_sum<kThreads>(s, s_sum);
-    b = block_sum_u64<kThreads>(b, s_bad);
-    f = block_sum_u64<kThreads>(f, s_bad);
-    if (f) b = kPartialTimeout;
-    // Non-finite logits gradients counted by the logits check since the last
-    // step (training.rs:228-241) skip this step like non-finite gradients:
-    // the reference applies the same transitions on both paths (:232-236,
-    // :294-298).  Folding the count into the rank partial makes every rank
-    // skip when any rank's logits were non-finite.
+    const Partial r = reduce_block_partials(p, gridDim.x);
     if (threadIdx.x == 0) {
+        // Non-finite logits gradients counted by the logits check since the
+        // last step (training.rs:228-241) skip this step like non-finite
+        // gradients: the reference applies the same transitions on both
+        // paths (:232-236, :294-298).  Folding the count into the rank
+        // partial makes every rank skip when any rank's logits were bad.
         const unsigned long long lb = atomicExch(p.logits_bad, 0ull);
-        if (b != kPartialTimeout) b += lb;
-    }
-    if (p.p2p) {
-        if (threadIdx.x == 0) {
-            s_sum[0] = s;
-            s_bad[0] = b;
-        }
-        __syncthreads();
-        if (threadIdx.x < kMaxP2PRanks) publish_partial_p2p(p, s_sum[0], s_bad[0]);
-    } else if (threadIdx.x == 0) {
-        p.part_local->sumsq = s;
-        p.part_local->nonfinite = b;   // threads that saw an inf/NaN (> 0 iff any)
+        p.part_local->sumsq = r.sumsq;
+        p.part_local->nonfinite = r.nonfinite == kPartialTimeout ? r.nonfinite : r.nonfinite + lb;
     }
 }
 
@@ -363,29 +374,43 @@ __device__ __forceinline__ uint4 p1_load(const uint4* p) {
     return r;
 }
 
-template <int U, bool KEEP, bool POW2, int LD>
-__device__ __forceinline__ void p1_stream(P1Acc& a, const P1Scale& sc, const StepParams& p) {
-    const uint4* g = reinterpret_cast<const uint4*>(p.g16);
-    const uint64_t nvec = p.n >> 3;
-    const uint64_t stride = (uint64_t)gridDim.x * kThreads;
-    uint64_t base = (uint64_t)blockIdx.x * kThreads + threadIdx.x;
-    for (; base + stride * (U - 1) < nvec; base += stride * U) {
-        uint4 q[U];
-#pragma unroll
-        for (int u = 0; u < U; ++u) q[u] = p1_load<LD>(g + base + u * stride);
-#pragma unroll
-        for (int u = 0; u < U; ++u) p1_consume<KEEP, POW2>(a, q[u], base + u * stride, sc, p);
-    }
-    uint4 q[U];
+template <int U, int LD>
+__device__ __forceinline__ void p1_load_round(uint4 (&q)[U], const uint4* g, uint64_t base,
+                                              uint64_t stride, uint64_t nvec) {
 #pragma unroll
     for (int u = 0; u < U; ++u) {
         const uint64_t i = base + u * stride;
         q[u] = i < nvec ? p1_load<LD>(g + i) : make_uint4(0, 0, 0, 0);
     }
+}
+
+// q holds this thread's first round, loaded before the loss scale was read.
+template <int U, bool KEEP, bool POW2, int LD>
+__device__ __forceinline__ void p1_stream(P1Acc& a, const P1Scale& sc, const StepParams& p,
+                                          uint4 (&q)[U]) {
+    const uint4* g = reinterpret_cast<const uint4*>(p.g16);
+    const uint64_t nvec = p.n >> 3;
+    const uint64_t stride = (uint64_t)gridDim.x * kThreads;
+    uint64_t base = (uint64_t)blockIdx.x * kThreads + threadIdx.x;
 #pragma unroll
     for (int u = 0; u < U; ++u) {
         const uint64_t i = base + u * stride;
         if (i < nvec) p1_consume<KEEP, POW2>(a, q[u], i, sc, p);
+    }
+    base += stride * U;
+    for (; base + stride * (U - 1) < nvec; base += stride * U) {
+#pragma unroll
+        for (int u = 0; u < U; ++u) q[u] = p1_load<LD>(g + base + u * stride);
+#pragma unroll
+        for (int u = 0; u < U; ++u) p1_consume<KEEP, POW2>(a, q[u], base + u * stride, sc, p);
+    }
+    if (base < nvec) {
+        p1_load_round<U, LD>(q, g, base, stride, nvec);
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const uint64_t i = base + u * stride;
+            if (i < nvec) p1_consume<KEEP, POW2>(a, q[u], i, sc, p);
+        }
     }
 }
 
@@ -393,10 +418,14 @@ __device__ __forceinline__ void p1_stream(P1Acc& a, const P1Scale& sc, const Ste
 template <int U, int MINB, bool KEEP, int LD>
 __global__ void __launch_bounds__(kThreads, MINB) pass1_kernel(StepParams p) {
     griddep_launch_dependents();
+    uint4 q[U];   // the first round goes out before the loss scale is read
+    p1_load_round<U, LD>(q, reinterpret_cast<const uint4*>(p.g16),
+                         (uint64_t)blockIdx.x * kThreads + threadIdx.x,
+                         (uint64_t)gridDim.x * kThreads, p.n >> 3);
     const P1Scale sc = p1_scale(p);
     P1Acc a;
-    if (sc.pow2) p1_stream<U, KEEP, true, LD>(a, sc, p);
-    else p1_stream<U, KEEP, false, LD>(a, sc, p);
+    if (sc.pow2) p1_stream<U, KEEP, true, LD>(a, sc, p, q);
+    else p1_stream<U, KEEP, false, LD>(a, sc, p, q);
     if (blockIdx.x == 0 && threadIdx.x < (p.n & 7u)) {   // ragged tail (n % 8)
         const uint64_t i = (p.n & ~7ull) + threadIdx.x;
         p1_consume1(a, p.g16[i], i, sc, p);
@@ -742,16 +771,31 @@ __global__ void __launch_bounds__(kThreads, MINB) pass2_kernel(StepParams p,
     P2Round<kUnroll2> r;
     p2_load<kUnroll2>(r, base, stride, nvec, g4, w4, m4, v4, g_early);
     griddep_wait();
-    if (p.p2p) {   // every rank's partial, from this rank's receive slots (bounded wait)
-        if (threadIdx.x < 32) gather_partials_p2p(p, s_part);
+    if (p.p1_last) {   // NCCL exchange: every rank's partial was all-gathered into part_all
+        if (threadIdx.x == 0) plan_from_partials(p, p.part_all, s_plan);
+    } else {
+        // this rank's partial: pass 1's block partials in a fixed order (the
+        // same value in every block), plus the non-finite logits count
+        Partial mine = reduce_block_partials(p, p.nblk1);
         if (threadIdx.x == 0) {
-            plan_from_partials(p, s_part, s_plan);
-            // a block that could not read a partial reports it (the last
-            // block folds it into the state); see gather_partials_p2p
-            if (s_plan.error) atomicExch(&p.st->error, s_plan.error);
+            if (mine.nonfinite != kPartialTimeout)
+                mine.nonfinite += *reinterpret_cast<volatile unsigned long long*>(p.logits_bad);
+            s_part[p.rank] = mine;
         }
-    } else if (threadIdx.x == 0) {
-        plan_from_partials(p, p.part_all, s_plan);
+        __syncthreads();
+        if (!p.p2p) {
+            if (threadIdx.x == 0) plan_from_partials(p, s_part, s_plan);
+        } else if (threadIdx.x < 32) {   // the peers' partials from this rank's slots
+            const Partial own = s_part[p.rank];
+            if (blockIdx.x == 0) publish_partial_p2p(p, s_plan.epoch, own);
+            gather_partials_p2p(p, s_plan.epoch, own, s_part);
+            if (threadIdx.x == 0) {
+                plan_from_partials(p, s_part, s_plan);
+                // a block that could not read a partial reports it (the last
+                // block folds it into the state); see gather_partials_p2p
+                if (s_plan.error) atomicExch(&p.st->error, s_plan.error);
+            }
+        }
     }
     __syncthreads();
     const Plan pl = s_plan;
@@ -784,7 +828,11 @@ __global__ void __launch_bounds__(kThreads, MINB) pass2_kernel(StepParams p,
     // peer stores of this block visible system-wide before it is counted
     if (GATHER) __threadfence_system();
     if (!last_block_arrived(p.ticket2, &s_last)) return;
-    if (threadIdx.x == 0) advance_state(p, pl);
+    if (threadIdx.x == 0) {
+        advance_state(p, pl);
+        // every block has read the logits count (before the ticket)
+        if (!p.p1_last) *p.logits_bad = 0ull;
+    }
     if (GATHER && p.p2p && threadIdx.x < p.world) {
         // weights-ready epoch into every rank's slot: every block's stores
         // into that rank's weight buffer precede it
@@ -1270,6 +1318,8 @@ StepParams make_params(const ark_opt_state* s, const uint16_t* g16) {
     p.part_local = s->d_part_local;
     p.part_all = s->d_part_all;
     p.verdict = s->d_verdict;
+    p.p1_last = (c.world_size > 1 && !s->p2p) ? 1 : 0;
+    p.nblk1 = 0;
     p.logits_bad = s->d_logits_bad;
     p.wdst = s->d_wdst;
     p.wself = 1;
@@ -1309,6 +1359,7 @@ int enqueue_step(ark_opt_state* s, cudaStream_t stream, uint16_t* w16, const uin
     // the caller's shard may live inside this rank's full weight buffer
     p.wself = !(gather && w16 == static_cast<uint16_t*>(s->wbuf) + s->cfg.shard_offset);
     if (ev) ARK_RECORD(ev[0], stream);
+    p.nblk1 = (unsigned int)(reduce ? s->blocks1r : s->blocks1);
     if (reduce) s->pass1r<<<s->blocks1r, kThreads, 0, stream>>>(p);
     else s->pass1<<<s->blocks1, kThreads, 0, stream>>>(p);
     ARK_CUDA_TRY(cudaGetLastError());
