@@ -724,9 +724,13 @@ __device__ __forceinline__ void p2_update(P2Round<U>& r, uint64_t base, uint64_t
             st_stream(w4 + i, r.wq[u]);
             if (GATHER) {   // every rank's full weight buffer: plain (peer) stores
                 const uint64_t gv = (p.offset >> 3) + i;
-                for (int q = 0; q < p.world; ++q)
-                    if (q != p.rank || p.wself)
-                        reinterpret_cast<uint4*>(p.wdst[q])[gv] = r.wq[u];
+                // the peer order starts at a different rank in each block, so
+                // the blocks of all ranks spread over every destination
+                int q = (int)(blockIdx.x % (unsigned)p.world);
+                for (int k = 0; k < p.world; ++k) {
+                    if (q != p.rank || p.wself) reinterpret_cast<uint4*>(p.wdst[q])[gv] = r.wq[u];
+                    if (++q == p.world) q = 0;
+                }
             }
             if (kW32) {   // the forward's FP32 weights (training.rs:165-186)
                 float4* o = reinterpret_cast<float4*>(p.w32_out) + 2 * i;
@@ -1506,7 +1510,10 @@ int ark_cuda_opt_init(const ark_opt_cfg* cfg, ark_opt_state** out) {
                                  (cfg->n >> 3) / kPass2Variants[varw].unroll + 1);
     s->pass1r = keep ? pass1_reduce_for<true>(cfg->world_size)
                      : pass1_reduce_for<false>(cfg->world_size);
-    const int shape_g = cfg->n < 100000000ull ? 0 : 1;
+    // fused weight all-gather: the plain kernel's shape by shard size (or
+    // by index through ARK_PASS2G_SHAPE: 0 = 1 group x 3 blocks/SM, 1 = 2 x 2)
+    int shape_g = cfg->n < 100000000ull ? 0 : 1;
+    if (const char* e = getenv("ARK_PASS2G_SHAPE")) shape_g = atoi(e) ? 1 : 0;
     s->pass2_gather = kPass2Gather[shape_g][keep];
     s->blocks2g = streaming_grid(reinterpret_cast<const void*>(s->pass2_gather), kThreads, 0,
                                  (cfg->n >> 3) / (shape_g ? 2 : 1) + 1);

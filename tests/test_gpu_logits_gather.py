@@ -162,3 +162,34 @@ def test_zero_grads_clears_the_handoff_buffer():
     torch.cuda.synchronize()
     assert int(full.view(torch.int16).ne(0).sum()) == 0
     opt.close()
+
+
+def test_gather_with_reduce_single_rank():
+    """ARK_STEP_REDUCE | ARK_STEP_GATHER_WEIGHTS: the hand-off, the update
+    and the weight all-gather in one step, against the hand-off step alone."""
+    L = layout.decoder_layout("gred", 2, 64, 160, 211)
+    n = L.n
+    sc = ab.LossScaleConfig(init=SCALE, every=50, max=2.0 ** 24)
+    ref = ab.Optimizer(L, ab.AdamConfig(**HP), sc, constant_lr=True, initial_step=3)
+    opt = ab.Optimizer(L, ab.AdamConfig(**HP), sc, constant_lr=True, initial_step=3)
+    rw, _, rm, rv = synth.make_state(n, 0, SEED, "cuda", loss_scale=SCALE)
+    w_full = opt.weight_buffer()
+    w_full.copy_(rw)
+    w16, m, v = w_full[opt.lo:opt.hi], rm.clone(), rv.clone()
+    rg_full, g_full = ref.grad_buffer(), opt.grad_buffer()
+    rshard = torch.zeros(n, dtype=torch.float16, device="cuda")
+    shard = torch.zeros(n, dtype=torch.float16, device="cuda")
+    for k in range(3):
+        synth.fill_f16(rg_full, 0, SEED, 0x500 + k, 1e-3, mult=SCALE)
+        g_full.copy_(rg_full)
+        ref.step_reduce(rw, rshard, rm, rv)
+        opt.step_gather(w16, shard, m, v, reduce=True)
+        opt.weights_wait()
+        torch.cuda.synchronize()
+        assert torch.equal(shard.view(torch.int16), rshard.view(torch.int16)), k
+        assert torch.equal(w_full.view(torch.int16), rw.view(torch.int16)), k
+    assert torch.equal(m.view(torch.int32), rm.view(torch.int32))
+    assert torch.equal(v.view(torch.int32), rv.view(torch.int32))
+    assert opt.status()["opt_step"] == ref.status()["opt_step"] == 6
+    ref.close()
+    opt.close()
