@@ -347,6 +347,7 @@ __device__ void p1_finish(const P1Acc& a, const P1Scale& sc, bool failed, const 
     if (!p.p1_last) return;
     if (!last_block_arrived(p.ticket1, &s_last)) return;
     const Partial r = reduce_block_partials(p, gridDim.x);
+    __shared__ Partial s_rank;
     if (threadIdx.x == 0) {
         // Non-finite logits gradients counted by the logits check since the
         // last step (training.rs:228-241) skip this step like non-finite
@@ -354,8 +355,14 @@ __device__ void p1_finish(const P1Acc& a, const P1Scale& sc, bool failed, const 
         // paths (:232-236, :294-298).  Folding the count into the rank
         // partial makes every rank skip when any rank's logits were bad.
         const unsigned long long lb = atomicExch(p.logits_bad, 0ull);
-        p.part_local->sumsq = r.sumsq;
-        p.part_local->nonfinite = r.nonfinite == kPartialTimeout ? r.nonfinite : r.nonfinite + lb;
+        Partial out = r;
+        if (out.nonfinite != kPartialTimeout) out.nonfinite += lb;
+        *p.part_local = out;
+        s_rank = out;
+    }
+    if (p.p2p) {   // publish to the peers now; pass 2 does the waiting
+        __syncthreads();
+        if (threadIdx.x < kMaxP2PRanks) publish_partial_p2p(p, p.st->steps_called + 1ull, s_rank);
     }
 }
 
@@ -633,6 +640,50 @@ __device__ void advance_state(const StepParams& p, const Plan& pl) {
     *p.st = st;
 }
 
+// The norm part of pass 2's plan, once per block after the grid-dependency
+// wait; every thread of the block calls it and on return the plan is in
+// s_plan for every thread.  P2RED: this rank's partial comes from reducing
+// pass 1's block partials here (a fixed order, the same value in every
+// block, plus the non-finite logits count), and block 0 publishes it to the
+// peers; otherwise pass 1's last block formed (and published) it.  With the
+// peer-to-peer exchange every block then reads the peers' partials from this
+// rank's slots (bounded); with the NCCL exchange they were all-gathered into
+// part_all.  P2RED is a template parameter so that the update kernel without
+// it keeps its register allocation (120 instead of 125 registers).
+template <bool P2RED>
+__device__ __forceinline__ void pass2_plan(const StepParams& p, Plan& s_plan, Partial* s_part) {
+    if (!P2RED && !p.p2p) {   // one GPU, or the NCCL all-gather into part_all
+        if (threadIdx.x == 0) plan_from_partials(p, p.part_all, s_plan);
+        __syncthreads();
+        return;
+    }
+    if (P2RED) {
+        Partial mine = reduce_block_partials(p, p.nblk1);
+        if (threadIdx.x == 0) {
+            if (mine.nonfinite != kPartialTimeout)
+                mine.nonfinite += *reinterpret_cast<volatile unsigned long long*>(p.logits_bad);
+            s_part[p.rank] = mine;
+        }
+    } else if (threadIdx.x == 0) {
+        s_part[p.rank] = *p.part_local;
+    }
+    __syncthreads();
+    if (!p.p2p) {
+        if (threadIdx.x == 0) plan_from_partials(p, s_part, s_plan);
+    } else if (threadIdx.x < 32) {   // the peers' partials from this rank's slots
+        const Partial own = s_part[p.rank];
+        if (P2RED && blockIdx.x == 0) publish_partial_p2p(p, s_plan.epoch, own);
+        gather_partials_p2p(p, s_plan.epoch, own, s_part);
+        if (threadIdx.x == 0) {
+            plan_from_partials(p, s_part, s_plan);
+            // a block that could not read a partial reports it (the last
+            // block folds it into the state); see gather_partials_p2p
+            if (s_plan.error) atomicExch(&p.st->error, s_plan.error);
+        }
+    }
+    __syncthreads();
+}
+
 // Eight elements of the update.  Without KEEP the compat kept range is
 // empty and no element index is compared for it.  DEC 1 turns the
 // weight-decay boundary n_decay into a count of decayed elements in this
@@ -755,7 +806,8 @@ __device__ __forceinline__ void p2_update(P2Round<U>& r, uint64_t base, uint64_t
 // 1's retire: before griddep_wait they form the state part of the plan and
 // load their first round of w, m, v (and g, unless pass 1 writes it: the
 // reduce-scatter step), none of which pass 1 writes.
-template <int kUnroll2, int MINB, bool kW32, bool KEEP, int DEC = 1, bool GATHER = false>
+template <int kUnroll2, int MINB, bool kW32, bool KEEP, int DEC = 1, bool GATHER = false,
+          bool P2RED = false>
 __global__ void __launch_bounds__(kThreads, MINB) pass2_kernel(StepParams p,
                                                               uint16_t* __restrict__ w16,
                                                               float* __restrict__ m,
@@ -775,33 +827,7 @@ __global__ void __launch_bounds__(kThreads, MINB) pass2_kernel(StepParams p,
     P2Round<kUnroll2> r;
     p2_load<kUnroll2>(r, base, stride, nvec, g4, w4, m4, v4, g_early);
     griddep_wait();
-    if (p.p1_last) {   // NCCL exchange: every rank's partial was all-gathered into part_all
-        if (threadIdx.x == 0) plan_from_partials(p, p.part_all, s_plan);
-    } else {
-        // this rank's partial: pass 1's block partials in a fixed order (the
-        // same value in every block), plus the non-finite logits count
-        Partial mine = reduce_block_partials(p, p.nblk1);
-        if (threadIdx.x == 0) {
-            if (mine.nonfinite != kPartialTimeout)
-                mine.nonfinite += *reinterpret_cast<volatile unsigned long long*>(p.logits_bad);
-            s_part[p.rank] = mine;
-        }
-        __syncthreads();
-        if (!p.p2p) {
-            if (threadIdx.x == 0) plan_from_partials(p, s_part, s_plan);
-        } else if (threadIdx.x < 32) {   // the peers' partials from this rank's slots
-            const Partial own = s_part[p.rank];
-            if (blockIdx.x == 0) publish_partial_p2p(p, s_plan.epoch, own);
-            gather_partials_p2p(p, s_plan.epoch, own, s_part);
-            if (threadIdx.x == 0) {
-                plan_from_partials(p, s_part, s_plan);
-                // a block that could not read a partial reports it (the last
-                // block folds it into the state); see gather_partials_p2p
-                if (s_plan.error) atomicExch(&p.st->error, s_plan.error);
-            }
-        }
-    }
-    __syncthreads();
+    pass2_plan<P2RED>(p, s_plan, s_part);
     const Plan pl = s_plan;
     if (!pl.skip) {
         if (!g_early) p2_load_g<kUnroll2>(r, base, stride, nvec, g4);
@@ -835,7 +861,7 @@ __global__ void __launch_bounds__(kThreads, MINB) pass2_kernel(StepParams p,
     if (threadIdx.x == 0) {
         advance_state(p, pl);
         // every block has read the logits count (before the ticket)
-        if (!p.p1_last) *p.logits_bad = 0ull;
+        if (P2RED) *p.logits_bad = 0ull;
     }
     if (GATHER && p.p2p && threadIdx.x < p.world) {
         // weights-ready epoch into every rank's slot: every block's stores
@@ -1000,7 +1026,9 @@ struct Pass1Variant {
 };
 struct Pass2Variant {
     int unroll, min_blocks;
-    Pass2Fn fn[2], fn_w32[2];   // [kept range non-empty]: plain / also writing FP32 weights
+    // [pass 2 reduces pass 1's block partials][kept range non-empty]:
+    // plain / also writing FP32 weights
+    Pass2Fn fn[2][2], fn_w32[2][2];
 };
 #define ARK_P1(U, B, L) {U, B, pass1_kernel<U, B, false, L>, pass1_kernel<U, B, true, L>}
 static const Pass1Variant kPass1Variants[] = {
@@ -1019,12 +1047,11 @@ static Pass1Fn pass1_reduce_for(int world) {
         default: return pass1_reduce_kernel<2, 4, KEEP>;
     }
 }
-#define ARK_P2(U, B)                                                                     \
-    {U, B, {pass2_kernel<U, B, false, false>, pass2_kernel<U, B, false, true>},            \
-     {pass2_kernel<U, B, true, false>, pass2_kernel<U, B, true, true>}}
-#define ARK_P2X(U, B, K, D)                                                              \
-    {U, B, {pass2_kernel<U, B, false, K, D>, pass2_kernel<U, B, false, true, D>},          \
-     {pass2_kernel<U, B, true, K, D>, pass2_kernel<U, B, true, true, D>}}
+#define ARK_P2S(U, B, W, K, D)                                                           \
+    {{pass2_kernel<U, B, W, K, D, false, false>, pass2_kernel<U, B, W, true, D, false, false>}, \
+     {pass2_kernel<U, B, W, K, D, false, true>, pass2_kernel<U, B, W, true, D, false, true>}}
+#define ARK_P2(U, B) {U, B, ARK_P2S(U, B, false, false, 1), ARK_P2S(U, B, true, false, 1)}
+#define ARK_P2X(U, B, K, D) {U, B, ARK_P2S(U, B, false, K, D), ARK_P2S(U, B, true, K, D)}
 // 5 and 6: the 2 x 2 shape with the kept-range check compiled in even when
 // the range is empty (5: decay chosen by two 64-bit boundary compares, 6: by
 // the per-vector count).  On B200 these are faster than 4 when the SM clock
@@ -1037,13 +1064,17 @@ static const Pass2Variant kPass2Variants[] = {
 };
 #undef ARK_P2X
 #undef ARK_P2
-// Pass 2 with the fused weight all-gather, [shape][kept range non-empty]:
-// shape 0 is 1 group x 3 blocks/SM (shards below 100M params), shape 1 is
-// 2 groups x 2 blocks/SM, as for the plain kernel.
-static const Pass2Fn kPass2Gather[2][2] = {
-    {pass2_kernel<1, 3, false, false, 1, true>, pass2_kernel<1, 3, false, true, 1, true>},
-    {pass2_kernel<2, 2, false, false, 1, true>, pass2_kernel<2, 2, false, true, 1, true>},
+#undef ARK_P2S
+// Pass 2 with the fused weight all-gather, [shape][pass-2 reduction][kept
+// range non-empty]: shape 0 is 1 group x 3 blocks/SM (shards below 100M
+// params), shape 1 is 2 groups x 2 blocks/SM, as for the plain kernel.
+#define ARK_P2G(U, B, R) \
+    {pass2_kernel<U, B, false, false, 1, true, R>, pass2_kernel<U, B, false, true, 1, true, R>}
+static const Pass2Fn kPass2Gather[2][2][2] = {
+    {ARK_P2G(1, 3, false), ARK_P2G(1, 3, true)},
+    {ARK_P2G(2, 2, false), ARK_P2G(2, 2, true)},
 };
+#undef ARK_P2G
 
 }  // namespace ark
 
@@ -1074,6 +1105,7 @@ struct ark_opt_state {
     Pass2Fn pass2 = nullptr, pass2_w32 = nullptr, pass2_gather = nullptr;
     int blocks2g = 0;
     bool pdl = false;  // pass 2 launched as a programmatic dependent of pass 1
+    bool p1_last = true;   // pass 1's last block forms the rank partial (else pass 2 does)
     int blocks2w = 0;
     // P2P exchange slots (world > 1)
     bool p2p = false;
@@ -1322,7 +1354,7 @@ StepParams make_params(const ark_opt_state* s, const uint16_t* g16) {
     p.part_local = s->d_part_local;
     p.part_all = s->d_part_all;
     p.verdict = s->d_verdict;
-    p.p1_last = (c.world_size > 1 && !s->p2p) ? 1 : 0;
+    p.p1_last = s->p1_last ? 1 : 0;
     p.nblk1 = 0;
     p.logits_bad = s->d_logits_bad;
     p.wdst = s->d_wdst;
@@ -1493,34 +1525,10 @@ int ark_cuda_opt_init(const ark_opt_cfg* cfg, ark_opt_state** out) {
     s->pass1 = keep ? kPass1Variants[var].fn_keep : kPass1Variants[var].fn;
     s->blocks1 = streaming_grid(reinterpret_cast<const void*>(s->pass1), kThreads, 0,
                                 (cfg->n >> 3) / kPass1Variants[var].unroll + 1);
-    // pass 2: 2 groups in flight x 2 blocks/SM (<= 128 registers) for large
-    // shards, 1 group x 3 blocks/SM below 100M params (shorter tail); from the
-    // B200 sweeps at the EKO, EKO/4 and EKO/8 shard sizes
-    int var2 = cfg->n < 100000000ull ? 1 : 4;
-    if (const char* e = getenv("ARK_PASS2_VARIANT")) var2 = atoi(e);
-    if (var2 < 0 || var2 >= (int)(sizeof(kPass2Variants) / sizeof(kPass2Variants[0]))) var2 = 0;
-    s->pass2 = kPass2Variants[var2].fn[keep];
-    // with the FP32 weight copy: 2 groups x 2 blocks/SM (<= 128 registers)
-    // is the fastest shape on B200 (EKO: 1.161 ms vs 1.237 ms for 1 x 3)
-    int varw = 4;
-    if (const char* e = getenv("ARK_PASS2W_VARIANT")) varw = atoi(e);
-    if (varw < 0 || varw >= (int)(sizeof(kPass2Variants) / sizeof(kPass2Variants[0]))) varw = 4;
-    s->pass2_w32 = kPass2Variants[varw].fn_w32[keep];
-    s->blocks2w = streaming_grid(reinterpret_cast<const void*>(s->pass2_w32), kThreads, 0,
-                                 (cfg->n >> 3) / kPass2Variants[varw].unroll + 1);
     s->pass1r = keep ? pass1_reduce_for<true>(cfg->world_size)
                      : pass1_reduce_for<false>(cfg->world_size);
-    // fused weight all-gather: the plain kernel's shape by shard size (or
-    // by index through ARK_PASS2G_SHAPE: 0 = 1 group x 3 blocks/SM, 1 = 2 x 2)
-    int shape_g = cfg->n < 100000000ull ? 0 : 1;
-    if (const char* e = getenv("ARK_PASS2G_SHAPE")) shape_g = atoi(e) ? 1 : 0;
-    s->pass2_gather = kPass2Gather[shape_g][keep];
-    s->blocks2g = streaming_grid(reinterpret_cast<const void*>(s->pass2_gather), kThreads, 0,
-                                 (cfg->n >> 3) / (shape_g ? 2 : 1) + 1);
     s->blocks1r = streaming_grid(reinterpret_cast<const void*>(s->pass1r), kThreads, 0,
                                  (cfg->n >> 3) + 1);
-    s->blocks2 = streaming_grid(reinterpret_cast<const void*>(s->pass2), kThreads, 0,
-                                (cfg->n >> 3) / kPass2Variants[var2].unroll + 1);
     const int W = cfg->world_size;
     s->timeout_ns = (uint64_t)(cfg->wait_timeout_ms ? cfg->wait_timeout_ms : 5000u) * 1000000ull;
     const int nblk = s->blocks1 > s->blocks1r ? s->blocks1 : s->blocks1r;
@@ -1584,6 +1592,41 @@ int ark_cuda_opt_init(const ark_opt_cfg* cfg, ark_opt_state** out) {
         }
         if (!s->p2p) teardown_p2p(s);   // every rank agreed to use the NCCL exchange
     }
+    // Who reduces pass 1's block partials into the rank partial.  Below 100M
+    // params per shard every pass-2 block does (pass 1 then has no serial
+    // last-block tail: 8-way EKO shard on B200, step 0.1265 -> 0.1211 ms);
+    // above, pass 1's last block does, overlapped by pass 2's prologue (the
+    // pass-2 reduction widens the update kernel's register allocation, 120
+    // -> 125, and measured 0.4 % slower on the 1.3B step).  The NCCL
+    // exchange always needs it in pass 1.  ARK_P1_LAST=0/1 forces either.
+    s->p1_last = cfg->n >= 100000000ull;
+    if (const char* e = getenv("ARK_P1_LAST")) s->p1_last = atoi(e) != 0;
+    if (W > 1 && !s->p2p) s->p1_last = true;
+    const int red = s->p1_last ? 0 : 1;
+    // pass 2: 2 groups in flight x 2 blocks/SM (<= 128 registers) for large
+    // shards, 1 group x 3 blocks/SM below 100M params (shorter tail); from the
+    // B200 sweeps at the EKO, EKO/4 and EKO/8 shard sizes
+    int var2 = cfg->n < 100000000ull ? 1 : 4;
+    if (const char* e = getenv("ARK_PASS2_VARIANT")) var2 = atoi(e);
+    if (var2 < 0 || var2 >= (int)(sizeof(kPass2Variants) / sizeof(kPass2Variants[0]))) var2 = 0;
+    s->pass2 = kPass2Variants[var2].fn[red][keep];
+    s->blocks2 = streaming_grid(reinterpret_cast<const void*>(s->pass2), kThreads, 0,
+                                (cfg->n >> 3) / kPass2Variants[var2].unroll + 1);
+    // with the FP32 weight copy: 2 groups x 2 blocks/SM (<= 128 registers)
+    // is the fastest shape on B200 (EKO: 1.161 ms vs 1.237 ms for 1 x 3)
+    int varw = 4;
+    if (const char* e = getenv("ARK_PASS2W_VARIANT")) varw = atoi(e);
+    if (varw < 0 || varw >= (int)(sizeof(kPass2Variants) / sizeof(kPass2Variants[0]))) varw = 4;
+    s->pass2_w32 = kPass2Variants[varw].fn_w32[red][keep];
+    s->blocks2w = streaming_grid(reinterpret_cast<const void*>(s->pass2_w32), kThreads, 0,
+                                 (cfg->n >> 3) / kPass2Variants[varw].unroll + 1);
+    // fused weight all-gather: the plain kernel's shape by shard size (or
+    // by index through ARK_PASS2G_SHAPE: 0 = 1 group x 3 blocks/SM, 1 = 2 x 2)
+    int shape_g = cfg->n < 100000000ull ? 0 : 1;
+    if (const char* e = getenv("ARK_PASS2G_SHAPE")) shape_g = atoi(e) ? 1 : 0;
+    s->pass2_gather = kPass2Gather[shape_g][red][keep];
+    s->blocks2g = streaming_grid(reinterpret_cast<const void*>(s->pass2_gather), kThreads, 0,
+                                 (cfg->n >> 3) / (shape_g ? 2 : 1) + 1);
     *out = s;
     return ARK_OK;
 }

@@ -82,7 +82,11 @@ def test_logits_check_scales_and_skips_like_the_reference(oracle):
     opt.close()
 
 
-def test_logits_check_empty_and_count_reset():
+@pytest.mark.parametrize("p1_last", ["0", "1"])
+def test_logits_check_empty_and_count_reset(p1_last, monkeypatch):
+    """With either side forming the rank partial (pass 2, or pass 1's last
+    block), which is also where the logits count is consumed."""
+    monkeypatch.setenv("ARK_P1_LAST", p1_last)
     L = layout.flat_layout(4096)
     opt = ab.Optimizer(L, ab.AdamConfig(**HP), ab.LossScaleConfig(init=SCALE), constant_lr=True)
     bufs = synth.make_state(L.n, 0, 3, "cuda", loss_scale=SCALE)

@@ -27,8 +27,11 @@ def _free_port():
     return p
 
 
-def _rank_main(rank, world, port, q, nccl_exchange):
+def _rank_main(rank, world, port, q, nccl_exchange, p1_last=None):
     import datetime
+
+    if p1_last is not None:   # who forms the rank partial: pass 1's last block or pass 2
+        os.environ["ARK_P1_LAST"] = p1_last
 
     import torch.distributed as dist
 
@@ -81,15 +84,16 @@ def _rank_main(rank, world, port, q, nccl_exchange):
 
 @pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason="needs 2 GPUs")
 @pytest.mark.parametrize("world", WORLDS)
-@pytest.mark.parametrize("nccl_exchange", [False, True])
-def test_multi_gpu_zero1_step_matches_oracle(oracle, nccl_exchange, world):
+@pytest.mark.parametrize("nccl_exchange,p1_last", [(False, None), (True, None), (False, "1")],
+                         ids=["p2p", "nccl", "p2p-p1last"])
+def test_multi_gpu_zero1_step_matches_oracle(oracle, nccl_exchange, p1_last, world):
     from ark_b200 import layout, synth
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     port = _free_port()
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=_rank_main, args=(r, world, port, q, nccl_exchange))
+    procs = [ctx.Process(target=_rank_main, args=(r, world, port, q, nccl_exchange, p1_last))
              for r in range(world)]
     for p in procs:
         p.start()

@@ -17,7 +17,10 @@ pytestmark = pytest.mark.gpu
 N_PASS1, N_PASS2 = 10, 7
 
 CASES = ([{"ARK_PDL": "0"}] + [{"ARK_PASS1_VARIANT": str(i)} for i in range(N_PASS1)] +
-         [{"ARK_PASS2_VARIANT": str(i)} for i in range(N_PASS2)])
+         [{"ARK_PASS2_VARIANT": str(i)} for i in range(N_PASS2)] +
+         # who reduces pass 1's block partials: pass 1's last block (1) or
+         # every pass-2 block (0), each with both pass-2 shapes
+         [{"ARK_P1_LAST": r, "ARK_PASS2_VARIANT": v} for r in ("0", "1") for v in ("1", "4")])
 
 
 def case_id(env):
@@ -43,10 +46,13 @@ def test_variant_compat_kept_range(oracle, env, monkeypatch):
     assert st["opt_step"] == 2
 
 
-@pytest.mark.parametrize("var", range(N_PASS2))
-def test_fp32_copy_variant(oracle, var, monkeypatch):
+@pytest.mark.parametrize("var,p1_last", [(v, None) for v in range(N_PASS2)] +
+                         [(4, "0"), (4, "1")])
+def test_fp32_copy_variant(oracle, var, p1_last, monkeypatch):
     """ARK_PASS2W_VARIANT: the step that also writes FP32 weights."""
     monkeypatch.setenv("ARK_PASS2W_VARIANT", str(var))
+    if p1_last is not None:
+        monkeypatch.setenv("ARK_P1_LAST", p1_last)
     L = layout.flat_layout(300_007)
     opt = ab.Optimizer(L, ab.AdamConfig(lr=3e-4, beta1=0.9, beta2=0.95, eps=1e-8,
                                         weight_decay=0.1, grad_clip=1.0),
