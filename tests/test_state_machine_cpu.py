@@ -131,3 +131,20 @@ def test_norm_is_exact_and_the_reference_fold_is_not(oracle):
     assert abs(fold - exact) / exact > 1e-4
     ref = np.sqrt(np.sum(g.astype(np.float64) ** 2))
     assert abs(ref - exact) / exact < 1e-12
+
+
+def test_logits_block_restatement(oracle):
+    """training.rs:228-245: any non-finite logits gradient rejects the step
+    before scaling (the buffer is left as it was); otherwise every value is
+    multiplied by the loss scale, one f32 multiply each."""
+    x = np.array([1.5, -2.25, 3e-8, 65504.0, 1e30], np.float32)
+    bad, y = oracle.logits_check_scale(x, 1024.0)
+    assert bad == 0
+    assert np.array_equal(y.view(np.uint32), (x * np.float32(1024.0)).view(np.uint32))
+    assert np.isinf(oracle.logits_check_scale(np.array([1e36], np.float32), 1e4)[1][0])
+    for poison in (np.nan, np.inf, -np.inf):
+        z = x.copy()
+        z[2] = poison
+        bad, y = oracle.logits_check_scale(z, 1024.0)
+        assert bad == 1 and np.array_equal(y.view(np.uint32), z.view(np.uint32))
+    assert oracle.logits_check_scale(np.zeros(0, np.float32), 2.0)[0] == 0
