@@ -262,11 +262,12 @@ ARK_API int ark_cuda_opt_step_ex(ark_opt_state* st, uint16_t* w16, uint16_t* g16
  * buffer until ark_cuda_opt_destroy. */
 ARK_API int ark_cuda_opt_weight_buffer(ark_opt_state* st, uint64_t n_full, uint16_t** w16_full);
 
-/* Enqueue on the state's stream a bounded wait until every rank's last
- * ARK_STEP_GATHER_WEIGHTS step has stored its shard into this rank's full
- * weight buffer; work enqueued after it on the stream reads the complete
- * updated weights.  A wait that runs out leaves ARK_E_TIMEOUT in the state.
- * No-op with world_size 1. */
+/* Enqueue on the state's stream a bounded wait until every rank's step of
+ * the same number has stored its shard into this rank's full weight buffer;
+ * work enqueued after it on the stream reads the complete updated weights.
+ * Call it after a step made with ARK_STEP_GATHER_WEIGHTS (on every rank):
+ * after any other step nothing is published and the wait runs out.  A wait
+ * that runs out leaves ARK_E_TIMEOUT in the state.  No-op with world_size 1. */
 ARK_API int ark_cuda_opt_weights_wait(ark_opt_state* st);
 
 /* Replaces the logits-gradient block of train_step (src/training.rs:228-245):
