@@ -132,9 +132,11 @@ ARK_API uint32_t    ark_cuda_abi_version(void);
  * decay applies to global indices [0, n_decay).
  *
  * Multi-GPU (ZeRO-1): rank r owns a contiguous shard; the only exchange is
- * a 16-byte {sum of squares, non-finite count} per rank, written by the last
- * block of pass 1 straight into the peers' memory over NVLink (or an NCCL
- * all-gather, see ARK_OPT_NCCL_EXCHANGE).
+ * a 16-byte {sum of squares, non-finite count} per rank, stored straight
+ * into the peers' memory over NVLink (by pass 1's last block for shards of
+ * 100M params and more, else by the update kernel) and read, with a bounded
+ * wait, by the update kernel (or an NCCL all-gather between the kernels,
+ * see ARK_OPT_NCCL_EXCHANGE).
  * ====================================================================== */
 
 /* Reproduce the reference's unscale omission for the final RMSNorm gain
